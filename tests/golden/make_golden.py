@@ -1,0 +1,207 @@
+"""Generate the golden fixtures in this folder by running the REFERENCE silogic.
+
+Run it in a container where the reference source tree is importable:
+
+    PYTHONPATH=<path to reference checkout> PYTHONDONTWRITEBYTECODE=1 \
+        python tests/golden/make_golden.py <path to reference checkout>
+
+Every case builds a network with the reference constructors, overwrites every
+learnable parameter with N(0, 1) draws from a seeded generator (so gate choices
+are not all the residual-init "A" gate), draws seeded inputs, and records
+
+* ``ctor`` / ``kwargs``: the constructor call (JSON) -- silogic_b200 exposes the
+  same classes, so a test rebuilds the net and loads ``sd/*``;
+* ``sd/<name>``: the full reference ``state_dict`` (parameters and buffers);
+* ``x``: the input batch;
+* ``hard``: ``model.forward_hard(x)`` -- integer GroupSum counts (float dtype);
+* ``feat``: the soft activations that enter the head (``model._run(x, False)``);
+* ``logits``: the soft forward ``model(x)`` (training mode, as in a train step);
+* ``grad/<name>``: gradients of ``(logits * R).sum()`` w.r.t. every parameter
+  (and ``grad/x`` w.r.t. the input where it is a leaf), ``R`` = ``rmat``.
+
+The reference is only imported here; nothing at test time reads it.
+"""
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+
+OUT_DIR = os.path.dirname(os.path.abspath(__file__))
+
+
+def _randomise(model, seed):
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for p in model.parameters():
+            p.copy_(torch.randn(p.shape, generator=g))
+
+
+def _bits(shape, seed, p=0.3):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.rand(shape, generator=g) < p).float()
+
+
+def _uniform(shape, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.rand(shape, generator=g)
+
+
+def _record(name, model, x, extra_pre=None, x_leaf=True, ctor=None, kwargs=None,
+            store=None, img_shape=None):
+    """Run hard + soft fwd/bwd on the reference and save an .npz fixture."""
+    import silogic  # noqa: F401  (reference)
+    store = {} if store is None else store
+    model.train()
+    with torch.no_grad():
+        xin = extra_pre.forward_hard(x) if extra_pre is not None else x
+        if extra_pre is not None:
+            xin = _encoded_to_image(xin, img_shape)
+        hard = model.forward_hard(xin)
+    xr = x.clone().requires_grad_(x_leaf)
+    xs = xr
+    if extra_pre is not None:
+        xs = _encoded_to_image(extra_pre(xr), img_shape)
+    feat = model._run(xs, hard=False)
+    logits = model.head(feat)
+    g = torch.Generator().manual_seed(12345)
+    rmat = torch.randn(logits.shape, generator=g)
+    (logits * rmat).sum().backward()
+    out = {
+        "ctor": np.array(ctor), "kwargs": np.array(json.dumps(kwargs)),
+        "x": x.numpy(), "hard": hard.numpy(), "feat": feat.detach().numpy(),
+        "logits": logits.detach().numpy(), "rmat": rmat.numpy(),
+    }
+    for k, v in model.state_dict().items():
+        out["sd/" + k] = v.numpy()
+    for k, p in model.named_parameters():
+        if p.grad is not None:
+            out["grad/" + k] = p.grad.numpy()
+    if extra_pre is not None:
+        for k, v in extra_pre.state_dict().items():
+            out["encsd/" + k] = v.numpy()
+        for k, p in extra_pre.named_parameters():
+            out["encgrad/" + k] = p.grad.numpy()
+    if x_leaf and xr.grad is not None:
+        out["grad/x"] = xr.grad.numpy()
+    out.update(store)
+    np.savez_compressed(os.path.join(OUT_DIR, name + ".npz"), **out)
+    print(f"{name}: hard {hard.shape} logits {logits.shape}")
+
+
+def _encoded_to_image(enc, shape):
+    """[B, C*H*W*bits] encoder output -> [B, C*bits, H, W], channel = c*bits + bit."""
+    B, C, H, W = shape
+    bits = enc.shape[1] // (C * H * W)
+    return enc.view(B, C, H, W, bits).permute(0, 1, 4, 2, 3).reshape(B, C * bits, H, W)
+
+
+def fc_cases():
+    from silogic.models import LogicNet
+    cases = [
+        ("fc_gate16_fixed", dict(in_dim=64, width=120, depth=3, node="gate16",
+                                 connectome="fixed", tau=10.0, seed=0)),
+        ("fc_gate16_topk", dict(in_dim=64, width=120, depth=3, node="gate16",
+                                connectome="topk", k=8, tau=10.0, seed=1)),
+        ("fc_gate16_topk_hardsel", dict(in_dim=64, width=120, depth=2, node="gate16",
+                                        connectome="topk", k=4, tau=10.0, seed=2,
+                                        gate_select="hard", wire_residual=0.25)),
+        ("fc_walsh_topk", dict(in_dim=64, width=120, depth=3, node="walsh",
+                               connectome="topk", k=8, tau=10.0, seed=3)),
+        ("fc_walsh_fixed_a3", dict(in_dim=64, width=120, depth=2, node="walsh",
+                                   arity=3, connectome="fixed", tau=10.0, seed=4,
+                                   node_tau=2.0)),
+        ("fc_multilinear_a2_ste", dict(in_dim=64, width=120, depth=2, node="multilinear",
+                                       connectome="topk", k=8, tau=10.0, seed=5,
+                                       gate_select="hard")),
+        ("fc_multilinear_a6", dict(in_dim=64, width=120, depth=2, node="multilinear",
+                                   arity=6, connectome="topk", k=3, tau=10.0, seed=6)),
+        ("fc_hybrid_a4", dict(in_dim=64, width=120, depth=2, node="hybrid", arity=4,
+                              connectome="topk", k=4, tau=10.0, seed=7)),
+        ("fc_hybrid_a3_fixed", dict(in_dim=64, width=120, depth=2, node="hybrid",
+                                    arity=3, connectome="fixed", tau=10.0, seed=8)),
+    ]
+    for i, (name, kw) in enumerate(cases):
+        torch.manual_seed(100 + i)
+        m = LogicNet(**kw)
+        _randomise(m, 200 + i)
+        x = _bits((100, 64), 300 + i)
+        _record(name, m, x, ctor="LogicNet", kwargs=kw)
+
+
+def conv_cases():
+    from silogic.models import LogicTreeNet, LogicConvNet
+    from silogic.encoders import LearnedThermometerEncoder
+    from silogic.data import binarize_spatial
+    cases = [
+        ("conv_gate16_topk_d2", "LogicTreeNet",
+         dict(in_channels=6, in_hw=8, channels=[16, 32], head_widths=[80],
+              tree_depth=2, node="gate16", tau=20.0, seed=0)),
+        ("conv_gate16_fixed_d2", "LogicTreeNet",
+         dict(in_channels=6, in_hw=8, channels=[16, 32], head_widths=[80],
+              tree_depth=2, node="gate16", connect="fixed", head_connect="fixed",
+              tau=20.0, seed=1)),
+        ("conv_gate16_topk_d3_wire", "LogicConvNet",
+         dict(in_channels=6, in_hw=8, channels=[16, 24], head_widths=[60, 40],
+              tree_depth=3, node="gate16", tau=5.0, seed=2, wire_residual=0.25,
+              gate_select="hard")),
+        ("conv_hybrid_a4_d1", "LogicConvNet",
+         dict(in_channels=6, in_hw=8, channels=[16, 32], head_widths=[80],
+              tree_depth=1, node="hybrid", arity=4, k=4, n_chan=2, tau=20.0, seed=3)),
+    ]
+    for i, (name, ctor, kw) in enumerate(cases):
+        torch.manual_seed(400 + i)
+        cls = {"LogicTreeNet": LogicTreeNet, "LogicConvNet": LogicConvNet}[ctor]
+        m = cls(**kw)
+        _randomise(m, 500 + i)
+        img = _uniform((40, 3, 8, 8), 600 + i)
+        x = binarize_spatial(img, [1 / 3, 2 / 3]).float()   # 6 channels
+        _record(name, m, x, x_leaf=True, ctor=ctor, kwargs=kw,
+                store={"img": img.numpy()})
+
+    # multilinear arity-6 conv with the learned thermometer encoder (C4 family)
+    torch.manual_seed(450)
+    kw = dict(in_channels=9, in_hw=8, channels=[16, 32], head_widths=[100, 100],
+              tree_depth=1, node="multilinear", arity=6, connect="topk", k=8,
+              n_chan=4, gate_select="hard", tau=12.0, seed=4)
+    m = LogicConvNet(**kw)
+    enc = LearnedThermometerEncoder(3 * 8 * 8, 3)
+    _randomise(m, 550)
+    img = _uniform((24, 3, 8, 8), 650)
+    x = img.reshape(24, -1)
+    _record("conv_multilinear_a6_enc", m, x, extra_pre=enc, x_leaf=True,
+            ctor="LogicConvNet", kwargs=kw, img_shape=(24, 3, 8, 8),
+            store={"enc_kwargs": np.array(json.dumps(dict(num_features=192, bits=3))),
+                   "img_shape": np.array([24, 3, 8, 8])})
+
+
+def prim_cases():
+    """Packing / GroupSum / thermometer known answers from the reference ops."""
+    from silogic.bitpacking.ops import pack_bits, group_sum_packed, n_words
+    from silogic.data import binarize_spatial, FIVE_THRESH
+    out = {}
+    rng = np.random.default_rng(7)
+    for B, F in [(1, 1), (63, 8), (64, 64), (65, 256), (200, 784)]:
+        x = rng.integers(0, 2, (B, F), dtype=np.uint8)
+        out[f"pack_{B}_{F}/x"] = x
+        out[f"pack_{B}_{F}/packed"] = pack_bits(x)
+    xs = rng.integers(0, 2, (130, 200), dtype=np.uint8)
+    p = pack_bits(xs)
+    out["gsum/x"] = xs
+    out["gsum/logits_tau4"] = group_sum_packed(p, 130, 10, 4.0)
+    out["nwords"] = np.array([n_words(b) for b in [1, 64, 65, 128, 129]])
+    img = torch.rand(5, 3, 6, 6, generator=torch.Generator().manual_seed(3))
+    img[0, 0, 0, :] = torch.tensor([1 / 6, 2 / 6, 3 / 6, 4 / 6, 5 / 6, 0.0])
+    out["thermo/img"] = img.numpy()
+    out["thermo/bits"] = binarize_spatial(img, FIVE_THRESH).numpy()
+    np.savez_compressed(os.path.join(OUT_DIR, "prims.npz"), **out)
+    print("prims written")
+
+
+if __name__ == "__main__":
+    if len(sys.argv) > 1:
+        sys.path.insert(0, sys.argv[1])
+    prim_cases()
+    fc_cases()
+    conv_cases()
