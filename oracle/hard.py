@@ -139,10 +139,36 @@ def eval_lut(operands, tt):
     return out
 
 
+# the 16 two-input functions by LUT code (bit p = output at a = p & 1, b = p >> 1),
+# as single numpy bitwise expressions (packed_layer.py:85-116, ops.py:123-140)
+_GATE2 = {
+    0b0000: lambda a, b: np.zeros_like(a), 0b1000: lambda a, b: a & b,
+    0b0010: lambda a, b: a & ~b, 0b1010: lambda a, b: a.copy(),
+    0b0100: lambda a, b: ~a & b, 0b1100: lambda a, b: b.copy(),
+    0b0110: lambda a, b: a ^ b, 0b1110: lambda a, b: a | b,
+    0b0001: lambda a, b: ~(a | b), 0b1001: lambda a, b: ~(a ^ b),
+    0b0101: lambda a, b: ~a, 0b1101: lambda a, b: ~a | b,
+    0b0011: lambda a, b: ~b, 0b1011: lambda a, b: a | ~b,
+    0b0111: lambda a, b: ~(a & b), 0b1111: lambda a, b: np.full_like(a, ALL),
+}
+
+
+def fc_forward_gate2(x, idx, tt):
+    """Arity-2 layer, outputs grouped by gate so each group is one bitwise op."""
+    code = (tt.astype(np.int64) << np.arange(4)).sum(1)
+    out = np.empty((idx.shape[0], x.shape[1]), dtype=np.uint64)
+    for c in np.unique(code):
+        rows = np.nonzero(code == c)[0]
+        out[rows] = _GATE2[int(c)](x[idx[rows, 0]], x[idx[rows, 1]])
+    return out
+
+
 def fc_forward(x, idx, tt, wire_r=0):
     """One FC layer on ``[in, nw]`` packed input."""
-    ops = [x[idx[:, j]] for j in range(idx.shape[1])]
-    y = eval_lut(ops, tt)
+    if idx.shape[1] == 2:
+        y = fc_forward_gate2(x, idx, tt)
+    else:
+        y = eval_lut([x[idx[:, j]] for j in range(idx.shape[1])], tt)
     if wire_r and x.shape[0] == y.shape[0]:                   # models.py:91-92
         y[:wire_r] = x[:wire_r]
     return y

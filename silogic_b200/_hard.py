@@ -1,0 +1,157 @@
+"""Host wrappers of the bit-packed CUDA kernels, and parameter -> truth-table conversion.
+
+Packed activations are int64 tensors ``[rows, ldw]`` (conv: ``[C, H, W, ldw]``)
+with ``ldw = ceil(B/64)`` rounded up to even; sample ``b`` is bit ``b % 64`` of
+word ``b // 64``, as in ``silogic/bitpacking/ops.py:32-49``.
+"""
+import torch
+
+from . import _lib
+from ._lib import call, ptr, require_cuda, stream_ptr
+from .functional import gate16_lut_codes
+
+_GATE_LUT = gate16_lut_codes()
+
+
+def n_words(B):
+    """Number of 64-sample words for ``B`` samples (``ops.py:27-29``)."""
+    return (int(B) + 63) >> 6
+
+
+def ldw_for(B):
+    nw = n_words(B)
+    return max(2, nw + (nw & 1))
+
+
+# ------------------------------------------------------------------ packing
+def pack(x, ldw=None):
+    """``[B, F]`` (uint8 / bool / float, nonzero-after-uint8-cast = 1) -> ``[F, ldw]`` int64."""
+    require_cuda(x)
+    B = x.shape[0]
+    x2 = x.reshape(B, -1)
+    F = x2.shape[1]
+    ldw = ldw or ldw_for(B)
+    out = torch.empty((F, ldw), dtype=torch.int64, device=x.device)
+    if x2.dtype == torch.bool:
+        x2 = x2.view(torch.uint8)
+    if x2.dtype == torch.uint8:
+        x2 = x2.contiguous()
+        call("slg_pack_u8", ptr(x2), B, F, ptr(out), ldw, stream_ptr(x.device))
+    else:
+        x2 = x2.float().contiguous()
+        call("slg_pack_f32", ptr(x2), B, F, ptr(out), ldw, stream_ptr(x.device))
+    return out
+
+
+def unpack(p, B):
+    """``[F, ldw]`` int64 -> ``[B, F]`` uint8."""
+    require_cuda(p)
+    p = p.contiguous()
+    F, ldw = p.shape[0], p.shape[-1]
+    F = p.numel() // ldw
+    out = torch.empty((B, F), dtype=torch.uint8, device=p.device)
+    call("slg_unpack_u8", ptr(p), F, ldw, B, ptr(out), stream_ptr(p.device))
+    return out
+
+
+def thermo_pack(img, thresholds, mode=0, ldw=None):
+    """Thermometer-encode ``[B, C, H, W]`` fp32 and pack to ``[C*T, H, W, ldw]``.
+
+    mode 0 = ``binarize_spatial`` (shared thresholds, channel ``t*C + c``);
+    mode 1 = learned encoder (per-feature thresholds ``[C*H*W, T]``, channel ``c*T + t``).
+    """
+    require_cuda(img)
+    B, C, H, W = img.shape
+    thr = torch.as_tensor(thresholds, dtype=torch.float32, device=img.device).contiguous()
+    T = thr.shape[-1] if thr.dim() else 1
+    ldw = ldw or ldw_for(B)
+    out = torch.empty((C * T, H, W, ldw), dtype=torch.int64, device=img.device)
+    x = img.float().contiguous()
+    call("slg_thermo_pack", ptr(x), B, C, H * W, ptr(thr), T, mode, ptr(out), ldw,
+         stream_ptr(img.device))
+    return out
+
+
+# ---------------------------------------------------------------- circuits
+def fc(x, idx, tt, wire_r=0, out=None):
+    """One FC hard layer: ``[in, ldw]`` -> ``[out, ldw]``."""
+    require_cuda(x)
+    in_dim, ldw = x.shape
+    out_dim, arity = idx.shape
+    if out is None:
+        out = torch.empty((out_dim, ldw), dtype=torch.int64, device=x.device)
+    call("slg_fc_hard", ptr(x), in_dim, ldw, ptr(idx), ptr(tt), arity, out_dim, wire_r,
+         ptr(out), stream_ptr(x.device))
+    return out
+
+
+def conv(x, leaf, tt, arity, depth, kernel=3, pad=1, wire_r=0, pool=2, out=None):
+    """One conv tree block (+ OR-pool): ``[C, H, W, ldw]`` -> ``[n, Ho/pool, Wo/pool, ldw]``."""
+    require_cuda(x)
+    C, H, W, ldw = x.shape
+    n = leaf.shape[0]
+    Ho, Wo = H + 2 * pad - kernel + 1, W + 2 * pad - kernel + 1
+    if out is None:
+        out = torch.empty((n, Ho // pool, Wo // pool, ldw), dtype=torch.int64, device=x.device)
+    call("slg_conv_hard", ptr(x), C, H, W, ldw, ptr(leaf), ptr(tt), arity, depth, kernel, pad,
+         n, wire_r, pool, ptr(out), stream_ptr(x.device))
+    return out
+
+
+def groupsum(x, B, num_classes, out=None):
+    """Per-sample, per-class popcounts ``[B, C]`` int32 of ``[width, ldw]`` packed rows."""
+    require_cuda(x)
+    width = x.numel() // x.shape[-1]
+    if out is None:
+        out = torch.empty((B, num_classes), dtype=torch.int32, device=x.device)
+    call("slg_groupsum", ptr(x), width, x.shape[-1], B, num_classes, ptr(out),
+         stream_ptr(x.device))
+    return out
+
+
+# ------------------------------------------------- parameters -> truth tables
+def _pack_tt(bits):
+    """``[..., P]`` bool -> ``[...]`` int64 with bit p set where ``bits[..., p]``."""
+    P = bits.shape[-1]
+    w = torch.ones(P, dtype=torch.int64, device=bits.device) << torch.arange(P, device=bits.device)
+    return (bits.to(torch.int64) * w).sum(-1)
+
+
+def _corners(n, device):
+    p = torch.arange(2 ** n, device=device).unsqueeze(1)
+    return (p >> torch.arange(n, device=device)) & 1        # [P, n]
+
+
+@torch.no_grad()
+def node_truth_tables(node, params, arity, mono_mask=None):
+    """Hard truth tables (int64, bit p = output at address sum_j in_j << j).
+
+    Mirrors each node's ``forward_hard`` evaluated at the 2^arity cube corners
+    (``silogic/nodes.py:101-106,153-156,184-189,232-233,266-268``; the corner
+    enumeration of ``bitpacking/convert.py:100-123``).
+    """
+    dev = params.device
+    if node == "gate16":
+        return _GATE_LUT.to(dev)[params.argmax(dim=-1)]
+    if node in ("multilinear", "hybrid"):
+        return _pack_tt(params > 0)
+    cb = _corners(arity, dev).to(torch.float32)              # [P, n]
+    P = 2 ** arity
+    if node == "walsh":
+        u = 2 * cb - 1
+        z = torch.zeros(params.shape[:-1] + (P,), dtype=torch.float32, device=dev)
+        for m in range(P):                                   # sum over monomials in order
+            mono = torch.ones(P, device=dev)
+            for j in range(arity):
+                if (m >> j) & 1:
+                    mono = mono * u[:, j]
+            z = z + params[..., m:m + 1].float() * mono
+        return _pack_tt(z > 0)
+    if node == "linear":
+        z = params[..., :1].float() + params[..., 1:].float() @ cb.t()
+        return _pack_tt(z >= 0)
+    if node == "polynomial":
+        mk = mono_mask.to(dev).float()                       # [M, n]
+        mono = torch.where(mk[None] > 0, cb[:, None, :], torch.ones_like(cb[:, None, :])).prod(-1)
+        return _pack_tt(params.float() @ mono.t() >= 0)
+    raise ValueError(f"no hard form for node {node!r}")

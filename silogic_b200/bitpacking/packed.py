@@ -1,0 +1,180 @@
+"""Bit-packed inference objects with the API of ``silogic/bitpacking/packed_model.py``,
+``packed_layer.py`` and ``kernels/triton_*.py`` -- all evaluated by the CUDA kernels.
+
+Inputs may be numpy arrays (copied to the GPU; results copied back to numpy, as
+the reference's CPU classes return) or CUDA tensors (results stay on the GPU).
+"""
+import numpy as np
+import torch
+
+from .. import _hard
+from ..functional import gate16_lut_codes
+
+
+def _dev(device=None):
+    return torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+
+
+def _as_cuda(x, device=None):
+    if isinstance(x, np.ndarray):
+        return torch.from_numpy(np.ascontiguousarray(x)).to(_dev(device), non_blocking=True)
+    return x
+
+
+def _packed_in(x, device=None):
+    """numpy/torch ``[rows, nw]`` int64 -> CUDA ``[rows, ldw]`` (ldw even), plus nw."""
+    was_np = isinstance(x, np.ndarray)
+    t = _as_cuda(x, device)
+    nw = t.shape[-1]
+    if nw % 2:
+        t = torch.nn.functional.pad(t, (0, 1))
+    return t.contiguous(), nw, was_np
+
+
+def _packed_out(t, nw, was_np):
+    t = t[..., :nw]
+    return t.cpu().numpy() if was_np else t
+
+
+class PackedFCLayer:
+    """One hard FC layer: wiring ``[out, arity]`` int32 + truth tables ``[out]`` int64."""
+
+    def __init__(self, idx, tt):
+        self.idx = idx.to(torch.int32).contiguous()
+        self.tt = tt.to(torch.int64).contiguous()
+        self.out_dim, self.arity = self.idx.shape
+
+    def forward(self, x):
+        """``[in, n_words]`` int64 (numpy or CUDA) -> ``[out, n_words]``."""
+        t, nw, was_np = _packed_in(x, self.idx.device)
+        return _packed_out(_hard.fc(t, self.idx, self.tt), nw, was_np)
+
+    __call__ = forward
+
+
+class BitpackedGPULayer(PackedFCLayer):
+    """Gate16 layer from gate codes (``triton_layer.py:124-149`` signature)."""
+
+    def __init__(self, gate_types, a_idx, b_idx, device="cuda"):
+        dev = torch.device(device)
+        g = torch.as_tensor(np.asarray(gate_types), dtype=torch.int64)
+        idx = torch.stack([torch.as_tensor(np.asarray(a_idx)), torch.as_tensor(np.asarray(b_idx))], 1)
+        super().__init__(idx.to(dev), gate16_lut_codes()[g].to(dev))
+        self.device = device
+
+    @classmethod
+    def from_fc_layer(cls, fc_layer, device="cuda"):
+        obj = cls.__new__(cls)
+        PackedFCLayer.__init__(obj, fc_layer.idx.to(device), fc_layer.tt.to(device))
+        obj.device = device
+        return obj
+
+
+class PackedConvLayer:
+    """One hard conv tree block: leaves ``[n, leaves]`` + truth tables ``[n, nodes]``."""
+
+    def __init__(self, leaf, tt, arity, depth, kernel, pad, cin, n):
+        self.leaf, self.tt = leaf.contiguous(), tt.contiguous()
+        self.arity, self.depth, self.kh, self.kw = arity, depth, kernel, kernel
+        self.padding, self.stride, self.cin, self.n_out = pad, 1, cin, n
+        self.n_leaves = leaf.shape[1]
+
+    def forward(self, x4, pool=2, wire_r=0):
+        """Packed ``[C, H, W, ldw]`` CUDA -> ``[n, Ho/pool, Wo/pool, ldw]``."""
+        return _hard.conv(x4, self.leaf, self.tt, self.arity, self.depth, self.kh,
+                          self.padding, wire_r, pool)
+
+    def forward_packed(self, x_3d):
+        """Reference form on an already-unfolded ``[P, L, nw]`` input (no pool):
+        the taps become 1x1 taps over ``P`` channels."""
+        t, nw, was_np = _packed_in(x_3d, self.leaf.device)
+        P, L, ldw = t.shape
+        y = _hard.conv(t.view(P, L, 1, ldw), self.leaf, self.tt, self.arity, self.depth,
+                       kernel=1, pad=0, wire_r=0, pool=1)
+        return _packed_out(y.view(self.n_out, L, ldw), nw, was_np)
+
+
+class BitpackedConvGPULayer(PackedConvLayer):
+    @classmethod
+    def from_cpu_layer(cls, layer, device="cuda"):
+        return cls(layer.leaf.to(device), layer.tt.to(device), layer.arity, layer.depth,
+                   layer.kh, layer.padding, layer.cin, layer.n_out)
+
+
+class PackedGroupSumHead:
+    def __init__(self, num_classes, tau=1.0):
+        self.num_classes, self.tau = num_classes, tau
+
+    def forward(self, x, B):
+        t, nw, was_np = _packed_in(x)
+        c = _hard.groupsum(t, B, self.num_classes).float() / self.tau
+        return c.cpu().numpy() if was_np else c
+
+
+class BitpackedNet:
+    """End-to-end bit-packed ``LogicNet`` on the GPU.  ``net(x)`` with ``x`` ``[B, in]``
+    uint8 -> ``[B, num_classes]`` float32 = counts / tau (``packed_model.py:75-102``)."""
+
+    def __init__(self, plan, head):
+        self.plan, self.head = plan, head
+        self.num_layers = len(plan.steps)
+
+    def forward(self, x):
+        was_np = isinstance(x, np.ndarray)
+        t = _as_cuda(x)
+        B = t.shape[0]
+        counts = self.plan.counts(t)
+        logits = counts.float() / self.head.tau
+        return logits.cpu().numpy() if was_np else logits
+
+    __call__ = forward
+
+    def counts(self, x):
+        """Integer counts ``[B, C]`` int32 on the GPU (no ``/tau``)."""
+        return self.plan.counts(_as_cuda(x))
+
+    def layer_summary(self):
+        rows = []
+        for i, st in enumerate(self.plan.steps):
+            rows.append({"layer": i, "mode": st["op"], "out_dim": int(st.get("idx", st.get("leaf")).shape[0])})
+        return rows
+
+
+class BitpackedConvNet(BitpackedNet):
+    """End-to-end bit-packed ``LogicConvNet``: ``[B, C, H, W]`` uint8 -> logits."""
+
+    @classmethod
+    def from_conv_net(cls, bp_conv_net, H_in=None, W_in=None, device="cuda"):
+        """Reference ``BitpackedConvGPUNet.from_conv_net`` signature: the net is already
+        GPU-resident, so this returns it (moved to ``device``)."""
+        return bp_conv_net
+
+
+BitpackedConvGPUNet = BitpackedConvNet
+
+
+def packed_unfold_gpu(x_3d, kh, kw, stride, padding, H_in, W_in):
+    """``[C, H*W, nw]`` -> ``[C*kh*kw, L_out, nw]`` (API utility; the fused conv kernel
+    never materialises this)."""
+    C, L, nw = x_3d.shape
+    Ho = (H_in + 2 * padding - kh) // stride + 1
+    Wo = (W_in + 2 * padding - kw) // stride + 1
+    x4 = torch.nn.functional.pad(x_3d.view(C, H_in, W_in, nw), (0, 0, padding, padding, padding, padding))
+    cols = []
+    for dy in range(kh):
+        for dx in range(kw):
+            cols.append(x4[:, dy:dy + stride * Ho:stride, dx:dx + stride * Wo:stride])
+    return torch.stack(cols, 1).reshape(C * kh * kw, Ho * Wo, nw)
+
+
+def packed_or_pool_gpu(x_3d, H, W, pool_size=2):
+    """OR-pool ``[C, H*W, nw]`` -> ``[C, (H/ps)*(W/ps), nw]`` (API utility)."""
+    C, L, nw = x_3d.shape
+    ps = pool_size
+    x4 = x_3d.view(C, H, W, nw)[:, :H // ps * ps, :W // ps * ps]
+    x5 = x4.reshape(C, H // ps, ps, W // ps, ps, nw)
+    out = x5[:, :, 0, :, 0]
+    for dy in range(ps):
+        for dx in range(ps):
+            out = out | x5[:, :, dy, :, dx]
+    return out.reshape(C, -1, nw)

@@ -1,0 +1,87 @@
+"""Hard-circuit execution plan: a trained network flattened into a list of kernel
+launches over bit-packed activations (the device-side form of
+``silogic/bitpacking/convert.py`` + ``packed_model.py``).
+
+Packed activations never leave the GPU between layers; a conv block and its
+OR-pool are one launch; GroupSum is a popcount kernel.
+"""
+import torch
+
+from .. import _hard
+
+
+class HardPlan:
+    """Wiring + truth tables of every layer, on the parameters' device."""
+
+    def __init__(self, steps, in_shape, num_classes, tau):
+        self.steps = steps            # list of dicts, see from_model
+        self.in_shape = in_shape      # ("fc", F) or ("conv", C, H, W)
+        self.num_classes = num_classes
+        self.tau = tau
+
+    # ----------------------------------------------------------- building
+    @classmethod
+    @torch.no_grad()
+    def from_model(cls, model):
+        from ..models import LogicNet, LogicConvNet
+        steps = []
+        if isinstance(model, LogicNet):
+            d_in = model.layers[0].in_dim
+            for layer in model.layers:
+                idx, tt = layer.hard_spec()
+                wr = model.wire_r if (model.wire_r and layer.in_dim == layer.out_dim) else 0
+                steps.append(dict(op="fc", idx=idx, tt=tt, wire_r=wr))
+            in_shape = ("fc", d_in)
+        elif isinstance(model, LogicConvNet):
+            convs = [b for b in model.blocks[0::2]]
+            pools = [b for b in model.blocks[1::2]]
+            first = convs[0]
+            for conv, pool in zip(convs, pools):
+                leaf, tt = conv.hard_spec()
+                steps.append(dict(op="conv", leaf=leaf, tt=tt, arity=conv.node_arity,
+                                  depth=conv.d, kernel=conv.kh, pad=conv.padding,
+                                  wire_r=model.wire_channels(conv, conv.cin), pool=pool.size,
+                                  n=conv.n))
+            for layer in model.head_layers:
+                idx, tt = layer.hard_spec()
+                steps.append(dict(op="fc", idx=idx, tt=tt, wire_r=0))
+            in_shape = ("conv", first.cin, None, None)
+        else:
+            raise TypeError(f"unsupported model {type(model).__name__}")
+        head = model.head
+        nc = getattr(head, "num_classes", None)
+        tau = getattr(head, "tau", 1.0)
+        return cls(steps, in_shape, nc, tau)
+
+    # ---------------------------------------------------------- execution
+    def pack_input(self, x):
+        """Pack a binary input batch (``[B, F]`` or ``[B, C, H, W]``)."""
+        B = x.shape[0]
+        h = _hard.pack(x.reshape(B, -1))
+        if x.dim() == 4:
+            h = h.view(x.shape[1], x.shape[2], x.shape[3], -1)
+        return h
+
+    def run_packed(self, h):
+        """Run every layer on packed input ``h``; returns packed ``[width, ldw]``."""
+        for st in self.steps:
+            if st["op"] == "fc":
+                if h.dim() != 2:
+                    h = h.reshape(-1, h.shape[-1])
+                h = _hard.fc(h, st["idx"], st["tt"], st["wire_r"])
+            else:
+                h = _hard.conv(h, st["leaf"], st["tt"], st["arity"], st["depth"], st["kernel"],
+                               st["pad"], st["wire_r"], st["pool"])
+        return h.reshape(-1, h.shape[-1])
+
+    def counts(self, x):
+        """Integer GroupSum counts ``[B, num_classes]`` (int32) of binary input ``x``."""
+        B = x.shape[0]
+        return _hard.groupsum(self.run_packed(self.pack_input(x)), B, self.num_classes)
+
+    def counts_from_packed(self, h, B):
+        return _hard.groupsum(self.run_packed(h), B, self.num_classes)
+
+    def features(self, x):
+        """Last-layer bits ``[B, width]`` uint8."""
+        return _hard.unpack(self.run_packed(self.pack_input(x)), x.shape[0])

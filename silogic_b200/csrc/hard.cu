@@ -1,0 +1,271 @@
+// Hard (bit-packed) circuit kernels: FC LUT layer, conv logic tree + OR-pool,
+// GroupSum popcount.  All integer work; HBM/L2 bound, no tensor cores.
+//
+// Every thread moves 128 samples at once (one 16-byte uint4 = 4 x 32-bit words),
+// so each warp reads/writes whole 512-byte row segments.  The node (or output
+// channel) is uniform over groups of VT consecutive lanes, so wiring indices and
+// truth tables are broadcast loads and a node's gate never diverges.
+#include "common.cuh"
+
+namespace slg {
+
+constexpr int HB_THREADS = 256;
+
+// lanes per node along the word axis: power of two, <= 32, >= nvec when small
+static inline int pick_vt(int64_t nvec) {
+    int vt = 1;
+    while (vt < 32 && vt < nvec) vt <<= 1;
+    return vt;
+}
+
+// ----------------------------------------------------------------- FC layer
+template <int AR>
+__global__ void __launch_bounds__(HB_THREADS)
+fc_hard_kernel(const uint4* __restrict__ x, int64_t nvec, const int32_t* __restrict__ idx,
+               const uint64_t* __restrict__ tt, int64_t out_dim, int64_t wire_r,
+               uint4* __restrict__ out, int vt_shift) {
+    const int vt = 1 << vt_shift;
+    const int64_t o = (int64_t)blockIdx.x * (HB_THREADS >> vt_shift) + (threadIdx.x >> vt_shift);
+    const int64_t v = (int64_t)blockIdx.y * vt + (threadIdx.x & (vt - 1));
+    if (o >= out_dim || v >= nvec) return;
+    uint4 r;
+    if (o < wire_r) {
+        r = __ldg(&x[o * nvec + v]);
+    } else {
+        uint4 in[AR];
+#pragma unroll
+        for (int j = 0; j < AR; ++j) {
+            const int64_t row = __ldg(&idx[o * AR + j]);
+            in[j] = __ldg(&x[row * nvec + v]);
+        }
+        const uint64_t t = __ldg(&tt[o]);
+        uint32_t res[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            uint32_t vv[AR];
+#pragma unroll
+            for (int j = 0; j < AR; ++j) vv[j] = u4get(in[j], c);
+            res[c] = lut_eval<AR>(vv, t);
+        }
+        r = make_uint4(res[0], res[1], res[2], res[3]);
+    }
+    out[o * nvec + v] = r;
+}
+
+// ------------------------------------------------------------- conv tree
+// One thread: output channel n, one pooled output position, 128 samples.
+template <int AR, int DEPTH>
+struct Tree {
+    static constexpr int LEAVES = (DEPTH == 1) ? AR : (DEPTH == 2 ? AR * AR : (DEPTH == 3 ? AR * AR * AR : AR * AR * AR * AR));
+    static constexpr int NODES = (LEAVES - 1) / (AR - 1);
+};
+
+template <int AR, int DEPTH>
+__global__ void __launch_bounds__(HB_THREADS)
+conv_hard_kernel(const uint4* __restrict__ x, int64_t cin, int H, int W, int64_t nvec,
+                 const int32_t* __restrict__ leaf, const uint64_t* __restrict__ tt, int kernel,
+                 int pad, int64_t n_out, int64_t wire_r, int pool, int Hp, int Wp,
+                 uint4* __restrict__ out, int vt_shift) {
+    constexpr int LEAVES = Tree<AR, DEPTH>::LEAVES;
+    constexpr int NODES = Tree<AR, DEPTH>::NODES;
+    const int vt = 1 << vt_shift;
+    const int ppb = HB_THREADS >> vt_shift;  // positions per block
+    const int64_t npos = (int64_t)Hp * Wp;
+    const int64_t tiles = (npos + ppb - 1) / ppb;
+    const int64_t n = blockIdx.x / tiles;
+    const int64_t pos = (blockIdx.x % tiles) * ppb + (threadIdx.x >> vt_shift);
+    const int64_t v = (int64_t)blockIdx.y * vt + (threadIdx.x & (vt - 1));
+    if (n >= n_out || pos >= npos || v >= nvec) return;
+    const int py = (int)(pos / Wp), px = (int)(pos % Wp);
+    const int kk = kernel * kernel;
+
+    int lc[LEAVES], ly[LEAVES], lx[LEAVES];
+#pragma unroll
+    for (int l = 0; l < LEAVES; ++l) {
+        int r = __ldg(&leaf[n * LEAVES + l]);
+        lc[l] = r / kk;
+        ly[l] = (r % kk) / kernel - pad;
+        lx[l] = r % kernel - pad;
+    }
+    uint64_t tn[NODES];
+#pragma unroll
+    for (int i = 0; i < NODES; ++i) tn[i] = __ldg(&tt[n * NODES + i]);
+
+    uint4 acc = make_uint4(0, 0, 0, 0);
+    for (int oy = 0; oy < pool; ++oy) {
+        for (int ox = 0; ox < pool; ++ox) {
+            const int y = py * pool + oy, xx = px * pool + ox;
+            uint4 res;
+            if (n < wire_r) {
+                res = __ldg(&x[((n * H + y) * (int64_t)W + xx) * nvec + v]);
+            } else {
+                uint32_t val[LEAVES][4];
+#pragma unroll
+                for (int l = 0; l < LEAVES; ++l) {
+                    const int iy = y + ly[l], ix = xx + lx[l];
+                    uint4 u = make_uint4(0, 0, 0, 0);
+                    if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+                        u = __ldg(&x[((lc[l] * (int64_t)H + iy) * W + ix) * nvec + v]);
+                    val[l][0] = u.x; val[l][1] = u.y; val[l][2] = u.z; val[l][3] = u.w;
+                }
+                // bottom-up: level i has LEAVES / AR^(i+1) nodes
+                int width = LEAVES, node_base = 0;
+#pragma unroll
+                for (int lev = 0; lev < DEPTH; ++lev) {
+                    const int nn = width / AR;
+#pragma unroll
+                    for (int m = 0; m < nn; ++m) {
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            uint32_t vv[AR];
+#pragma unroll
+                            for (int j = 0; j < AR; ++j) vv[j] = val[m * AR + j][c];
+                            val[m][c] = lut_eval<AR>(vv, tn[node_base + m]);
+                        }
+                    }
+                    node_base += nn;
+                    width = nn;
+                }
+                res = make_uint4(val[0][0], val[0][1], val[0][2], val[0][3]);
+            }
+            acc.x |= res.x; acc.y |= res.y; acc.z |= res.z; acc.w |= res.w;
+        }
+    }
+    out[(n * npos + pos) * nvec + v] = acc;
+}
+
+// --------------------------------------------------------------- GroupSum
+// One thread: class c, one 32-bit word (32 samples).  Bit-sliced vertical
+// counters: plane l holds bit l of every sample's running count, so adding a
+// row costs a short carry ripple instead of 32 per-sample adds.
+__global__ void __launch_bounds__(HB_THREADS)
+groupsum_kernel(const uint32_t* __restrict__ x, int64_t G, int64_t ld32, int64_t B, int C,
+                int32_t* __restrict__ counts) {
+    const int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int c = blockIdx.y;
+    if (w * 32 >= B) return;
+    uint32_t plane[20];
+#pragma unroll
+    for (int l = 0; l < 20; ++l) plane[l] = 0;
+    const uint32_t* base = x + (int64_t)c * G * ld32 + w;
+    for (int64_t g = 0; g < G; ++g) {
+        uint32_t carry = __ldg(base + g * ld32);
+#pragma unroll
+        for (int l = 0; l < 20; ++l) {
+            const uint32_t t = plane[l] & carry;
+            plane[l] ^= carry;
+            carry = t;
+        }
+    }
+    const int64_t s_end = min((int64_t)32, B - w * 32);
+    for (int s = 0; s < s_end; ++s) {
+        int32_t cnt = 0;
+#pragma unroll
+        for (int l = 0; l < 20; ++l) cnt |= (int32_t)((plane[l] >> s) & 1u) << l;
+        counts[(w * 32 + s) * C + c] = cnt;
+    }
+}
+
+}  // namespace slg
+
+using namespace slg;
+
+extern "C" int slg_fc_hard(const uint64_t* x, int64_t in_dim, int64_t ldw, const int32_t* idx,
+                           const uint64_t* tt, int32_t arity, int64_t out_dim, int64_t wire_r,
+                           uint64_t* out, void* stream) {
+    if (in_dim <= 0 || out_dim < 0 || ldw <= 0 || wire_r < 0)
+        return set_error(SLG_ERR_ARG, "slg_fc_hard: bad sizes");
+    if (ldw & 1) return set_error(SLG_ERR_ALIGN, "slg_fc_hard: ldw must be even");
+    if (!aligned16(x) || !aligned16(out)) return set_error(SLG_ERR_ALIGN, "slg_fc_hard: x/out not 16-byte aligned");
+    if (wire_r > 0 && (wire_r > in_dim || wire_r > out_dim))
+        return set_error(SLG_ERR_ARG, "slg_fc_hard: wire_r exceeds a width");
+    if (out_dim == 0) return SLG_OK;
+    if (!idx || !tt) return set_error(SLG_ERR_ARG, "slg_fc_hard: null pointer");
+    const int64_t nvec = ldw / 2;
+    const int vt = pick_vt(nvec);
+    int vs = 0;
+    while ((1 << vs) < vt) ++vs;
+    const int64_t npb = HB_THREADS / vt;
+    const int64_t gy = cdiv(nvec, vt);
+    if (gy > 65535) return set_error(SLG_ERR_ARG, "slg_fc_hard: batch too large");
+    dim3 grid((unsigned)cdiv(out_dim, npb), (unsigned)gy);
+    auto xs = reinterpret_cast<const uint4*>(x);
+    auto os = reinterpret_cast<uint4*>(out);
+    cudaStream_t st = as_stream(stream);
+    switch (arity) {
+        case 1: fc_hard_kernel<1><<<grid, HB_THREADS, 0, st>>>(xs, nvec, idx, tt, out_dim, wire_r, os, vs); break;
+        case 2: fc_hard_kernel<2><<<grid, HB_THREADS, 0, st>>>(xs, nvec, idx, tt, out_dim, wire_r, os, vs); break;
+        case 3: fc_hard_kernel<3><<<grid, HB_THREADS, 0, st>>>(xs, nvec, idx, tt, out_dim, wire_r, os, vs); break;
+        case 4: fc_hard_kernel<4><<<grid, HB_THREADS, 0, st>>>(xs, nvec, idx, tt, out_dim, wire_r, os, vs); break;
+        case 5: fc_hard_kernel<5><<<grid, HB_THREADS, 0, st>>>(xs, nvec, idx, tt, out_dim, wire_r, os, vs); break;
+        case 6: fc_hard_kernel<6><<<grid, HB_THREADS, 0, st>>>(xs, nvec, idx, tt, out_dim, wire_r, os, vs); break;
+        default: return set_error(SLG_ERR_UNSUPPORTED, "slg_fc_hard: arity %d not in 1..6", arity);
+    }
+    return check_launch("slg_fc_hard");
+}
+
+template <int AR, int D>
+static void launch_conv(dim3 g, cudaStream_t st, const uint4* x, int64_t cin, int H, int W,
+                        int64_t nvec, const int32_t* leaf, const uint64_t* tt, int kernel, int pad,
+                        int64_t n_out, int64_t wire_r, int pool, int Hp, int Wp, uint4* out, int vs) {
+    conv_hard_kernel<AR, D><<<g, HB_THREADS, 0, st>>>(x, cin, H, W, nvec, leaf, tt, kernel, pad, n_out,
+                                                      wire_r, pool, Hp, Wp, out, vs);
+}
+
+extern "C" int slg_conv_hard(const uint64_t* x, int64_t cin, int64_t H, int64_t W, int64_t ldw,
+                             const int32_t* leaf, const uint64_t* tt, int32_t arity, int32_t depth,
+                             int32_t kernel, int32_t pad, int64_t n_out, int64_t wire_r, int32_t pool,
+                             uint64_t* out, void* stream) {
+    if (cin <= 0 || H <= 0 || W <= 0 || ldw <= 0 || n_out < 0 || kernel <= 0 || pad < 0 || wire_r < 0)
+        return set_error(SLG_ERR_ARG, "slg_conv_hard: bad sizes");
+    if (pool != 1 && pool != 2) return set_error(SLG_ERR_UNSUPPORTED, "slg_conv_hard: pool must be 1 or 2");
+    if (ldw & 1) return set_error(SLG_ERR_ALIGN, "slg_conv_hard: ldw must be even");
+    if (!aligned16(x) || !aligned16(out)) return set_error(SLG_ERR_ALIGN, "slg_conv_hard: x/out not 16-byte aligned");
+    const int64_t Ho = H + 2 * pad - kernel + 1, Wo = W + 2 * pad - kernel + 1;
+    if (Ho <= 0 || Wo <= 0) return set_error(SLG_ERR_ARG, "slg_conv_hard: empty output");
+    if (wire_r > 0 && (wire_r > cin || wire_r > n_out || Ho > H || Wo > W))
+        return set_error(SLG_ERR_ARG, "slg_conv_hard: wire_r needs cin >= wire_r and same-size output");
+    const int64_t Hp = Ho / pool, Wp = Wo / pool;
+    if (n_out == 0 || Hp == 0 || Wp == 0) return SLG_OK;
+    if (!leaf || !tt) return set_error(SLG_ERR_ARG, "slg_conv_hard: null pointer");
+    const int64_t nvec = ldw / 2;
+    const int vt = pick_vt(nvec);
+    int vs = 0;
+    while ((1 << vs) < vt) ++vs;
+    const int64_t ppb = HB_THREADS / vt;
+    const int64_t tiles = cdiv(Hp * Wp, ppb);
+    const int64_t gy = cdiv(nvec, vt);
+    if (gy > 65535 || n_out * tiles > 0x7fffffffLL) return set_error(SLG_ERR_ARG, "slg_conv_hard: grid too large");
+    dim3 grid((unsigned)(n_out * tiles), (unsigned)gy);
+    auto xs = reinterpret_cast<const uint4*>(x);
+    auto os = reinterpret_cast<uint4*>(out);
+    cudaStream_t st = as_stream(stream);
+    const int key = arity * 10 + depth;
+#define SLG_CONV_CASE(A, D) \
+    case A * 10 + D: launch_conv<A, D>(grid, st, xs, cin, (int)H, (int)W, nvec, leaf, tt, kernel, pad, n_out, wire_r, pool, (int)Hp, (int)Wp, os, vs); break;
+    switch (key) {
+        SLG_CONV_CASE(2, 1) SLG_CONV_CASE(2, 2) SLG_CONV_CASE(2, 3) SLG_CONV_CASE(2, 4)
+        SLG_CONV_CASE(3, 1) SLG_CONV_CASE(3, 2) SLG_CONV_CASE(4, 1) SLG_CONV_CASE(4, 2)
+        SLG_CONV_CASE(5, 1) SLG_CONV_CASE(6, 1)
+        default: return set_error(SLG_ERR_UNSUPPORTED, "slg_conv_hard: arity %d depth %d not built", arity, depth);
+    }
+#undef SLG_CONV_CASE
+    return check_launch("slg_conv_hard");
+}
+
+extern "C" int slg_groupsum(const uint64_t* x, int64_t width, int64_t ldw, int64_t B,
+                            int32_t num_classes, int32_t* counts, void* stream) {
+    if (width <= 0 || B < 0 || num_classes <= 0 || ldw <= 0)
+        return set_error(SLG_ERR_ARG, "slg_groupsum: bad sizes");
+    if (width % num_classes) return set_error(SLG_ERR_ARG, "slg_groupsum: width %% num_classes != 0");
+    if (ldw < cdiv(B, 64)) return set_error(SLG_ERR_ARG, "slg_groupsum: ldw too small");
+    const int64_t G = width / num_classes;
+    if (G >= (1 << 20)) return set_error(SLG_ERR_UNSUPPORTED, "slg_groupsum: group too large");
+    if (B == 0) return SLG_OK;
+    if (!x || !counts) return set_error(SLG_ERR_ARG, "slg_groupsum: null pointer");
+    const int64_t nw32 = cdiv(B, 32);
+    dim3 grid((unsigned)cdiv(nw32, HB_THREADS), (unsigned)num_classes);
+    groupsum_kernel<<<grid, HB_THREADS, 0, as_stream(stream)>>>(
+        reinterpret_cast<const uint32_t*>(x), G, ldw * 2, B, num_classes, counts);
+    return check_launch("slg_groupsum");
+}

@@ -1,0 +1,154 @@
+"""Hard (bit-packed) circuit on the GPU vs the reference golden counts and the oracle."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import FIXTURES, build_model, encoder_image, load
+from oracle import hard as OH
+from oracle.spec import net_spec
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+@pytest.mark.parametrize("name", FIXTURES)
+def test_forward_hard_matches_reference_golden(name):
+    m, enc, z, _ = build_model(name, dev)
+    x = torch.from_numpy(z["x"]).to(dev)
+    if enc is not None:
+        x = encoder_image(enc.forward_hard(x), z)
+    got = m.forward_hard(x)
+    np.testing.assert_array_equal(got.cpu().numpy(), z["hard"])
+
+
+@pytest.mark.parametrize("name", FIXTURES)
+def test_bitpacked_api_matches_reference_golden(name):
+    from silogic_b200.bitpacking import convert_logic_net, convert_logic_conv_net
+    m, enc, z, _ = build_model(name, dev)
+    x = torch.from_numpy(z["x"]).to(dev)
+    if enc is not None:
+        x = encoder_image(enc.forward_hard(x), z)
+    conv = "conv" in name
+    bp = convert_logic_conv_net(m) if conv else convert_logic_net(m)
+    logits = bp(x.to(torch.uint8).cpu().numpy())                # numpy in -> numpy out
+    tau = m.head.tau
+    np.testing.assert_array_equal(np.rint(logits * tau), z["hard"])
+
+
+def _rand_fc(in_dim, width, depth, seed, **kw):
+    import silogic_b200 as S
+    torch.manual_seed(seed)
+    m = S.LogicNet(in_dim, width, depth, seed=seed, **kw)
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.copy_(torch.randn(p.shape, generator=g))
+    return m
+
+
+@pytest.mark.parametrize("B", [1, 63, 64, 65, 127, 128, 129, 1000, 4097])
+def test_fc_ragged_batches_vs_oracle(B):
+    m = _rand_fc(100, 300, 3, 7, node="walsh", connectome="topk", k=8, tau=10.0)
+    g = torch.Generator().manual_seed(B)
+    x = (torch.rand(B, 100, generator=g) < 0.3).float()
+    sd = {k: v.numpy() for k, v in m.state_dict().items()}
+    ref = OH.model_counts("LogicNet", dict(in_dim=100, width=300, depth=3, node="walsh",
+                                           connectome="topk", k=8, tau=10.0, seed=7), sd,
+                          x.numpy().astype(np.uint8))
+    got = m.to(dev).forward_hard(x.to(dev))
+    np.testing.assert_array_equal(got.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("arity", [1, 2, 3, 4, 5, 6])
+def test_fc_lut_arities_vs_oracle(arity):
+    node = "multilinear" if arity > 1 else "linear"
+    kw = dict(in_dim=64, width=200, depth=2, node=node, arity=arity, connectome="topk", k=3,
+              tau=1.0, seed=arity)
+    m = _rand_fc(64, 200, 2, arity, **{k: v for k, v in kw.items()
+                                       if k not in ("in_dim", "width", "depth", "seed")})
+    sd = {k: v.numpy() for k, v in m.state_dict().items()}
+    x = (torch.rand(333, 64, generator=torch.Generator().manual_seed(1)) < 0.5).float()
+    ref = OH.model_counts("LogicNet", kw, sd, x.numpy().astype(np.uint8))
+    got = m.to(dev).forward_hard(x.to(dev))
+    np.testing.assert_array_equal(got.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("depth,node,arity,connect", [
+    (1, "gate16", 2, "topk"), (2, "gate16", 2, "fixed"), (3, "gate16", 2, "topk"),
+    (4, "gate16", 2, "topk"), (1, "multilinear", 6, "topk"), (1, "hybrid", 4, "fixed"),
+    (2, "multilinear", 3, "topk"), (2, "walsh", 2, "topk")])
+def test_conv_trees_vs_oracle(depth, node, arity, connect):
+    import silogic_b200 as S
+    kw = dict(in_channels=6, in_hw=12, channels=[24, 40], head_widths=[120], tree_depth=depth,
+              node=node, arity=arity, connect=connect, k=4, tau=3.0, seed=depth)
+    torch.manual_seed(5)
+    m = S.LogicConvNet(**kw)
+    g = torch.Generator().manual_seed(9)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.copy_(torch.randn(p.shape, generator=g))
+    sd = {k: v.numpy() for k, v in m.state_dict().items()}
+    x = (torch.rand(150, 6, 12, 12, generator=g) < 0.5).float()
+    ref = OH.model_counts("LogicConvNet", kw, sd, x.numpy().astype(np.uint8))
+    got = m.to(dev).forward_hard(x.to(dev))
+    np.testing.assert_array_equal(got.cpu().numpy(), ref)
+
+
+def test_layer_level_forward_hard_vs_oracle():
+    import silogic_b200 as S
+    torch.manual_seed(3)
+    conv = S.ConvLogicTree(4, 8, tree_depth=2, connect="topk", seed=3)
+    with torch.no_grad():
+        for p in conv.parameters():
+            p.normal_()
+    x = (torch.rand(70, 4, 7, 9) < 0.5).float()
+    y = conv.to(dev).forward_hard(x.to(dev)).cpu().numpy()
+    leaf, tts = conv.cpu().hard_spec()
+    otts = [OH.node_truth_tables("gate16", p.detach().reshape(-1, 16).numpy(), 2).reshape(8, -1, 4)
+            for p in conv.gate_logits]
+    h = OH.pack_bits(x.numpy().reshape(70, -1)).reshape(4, 7, 9, -1)
+    ref = OH.conv_forward(h, leaf.numpy().astype(np.int64), otts, 2, pool=1)
+    ref = OH.unpack_bits(ref.reshape(-1, ref.shape[-1]), 70).reshape(70, 8, 7, 9)
+    np.testing.assert_array_equal(y, ref)
+
+
+def test_pack_unpack_and_thermometer_vs_golden():
+    from silogic_b200 import _hard
+    from silogic_b200.bitpacking import pack_bits, unpack_bits
+    z = load("prims")
+    for B, F in [(1, 1), (63, 8), (64, 64), (65, 256), (200, 784)]:
+        x = z[f"pack_{B}_{F}/x"]
+        p = pack_bits(x)
+        np.testing.assert_array_equal(p, z[f"pack_{B}_{F}/packed"])
+        np.testing.assert_array_equal(unpack_bits(p, B), x)
+        xf = torch.from_numpy(x).float().cuda()
+        np.testing.assert_array_equal(_hard.pack(xf)[:, :p.shape[1]].cpu().numpy(), p)
+    import silogic_b200 as S
+    bits = S.binarize_spatial(torch.from_numpy(z["thermo/img"]).cuda(), S.FIVE_THRESH)
+    np.testing.assert_array_equal(bits.cpu().numpy(), z["thermo/bits"])
+
+
+def test_groupsum_vs_golden():
+    from silogic_b200 import _hard
+    z = load("prims")
+    x = torch.from_numpy(z["gsum/x"]).cuda()
+    c = _hard.groupsum(_hard.pack(x), 130, 10)
+    np.testing.assert_array_equal((c.float() / 4.0).cpu().numpy(), z["gsum/logits_tau4"])
+
+
+def test_large_group_groupsum_vs_oracle():
+    from silogic_b200 import _hard
+    x = (torch.rand(1000, 20000) < 0.5)
+    c = _hard.groupsum(_hard.pack(x.cuda()), 1000, 10).cpu().numpy()
+    np.testing.assert_array_equal(c, x.view(1000, 10, 2000).sum(-1).numpy())
+
+
+def test_learned_thermometer_hard_vs_oracle():
+    import silogic_b200 as S
+    enc = S.LearnedThermometerEncoder(50, 3)
+    with torch.no_grad():
+        enc.thresholds.copy_(torch.rand(50, 3))
+    x = torch.rand(77, 50)
+    got = enc.cuda().forward_hard(x.cuda()).cpu().numpy()
+    ref = OH.learned_thermometer_bits(x.numpy(), enc.thresholds.detach().cpu().numpy())
+    np.testing.assert_array_equal(got, ref)

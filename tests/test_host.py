@@ -1,0 +1,69 @@
+"""Host-side logic on CPU: constructor parity (seeded wiring), state_dict layout,
+parameter -> truth-table conversion, plan building.  No kernel launches."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import FIXTURES, build_model, load
+from oracle import hard as OH
+from oracle.spec import net_spec
+from silogic_b200 import _hard
+
+
+@pytest.mark.parametrize("name", FIXTURES)
+def test_constructor_matches_reference_state_dict(name):
+    """Same seed -> identical wiring buffers and identical state_dict keys/shapes."""
+    m, enc, z, fresh = build_model(name)
+    ref_keys = {k[3:] for k in z.files if k.startswith("sd/")}
+    assert set(fresh) == ref_keys
+    for k, v in fresh.items():
+        ref = z["sd/" + k]
+        assert tuple(v.shape) == ref.shape, k
+        if v.dtype in (torch.int64, torch.int32) or k.endswith(("basis", "truth", "corners")):
+            np.testing.assert_array_equal(v.numpy(), ref, err_msg=k)
+
+
+@pytest.mark.parametrize("name", FIXTURES)
+def test_truth_tables_match_oracle(name):
+    m, enc, z, _ = build_model(name)
+    sd = {k[3:]: z[k] for k in z.files if k.startswith("sd/")}
+    spec = net_spec(str(z["ctor"]), str(z["kwargs"]), sd)
+    fc_layers = spec["layers"] if spec["type"] == "fc" else spec["head"]
+    mods = m.layers if spec["type"] == "fc" else m.head_layers
+    for L, mod in zip(fc_layers, mods):
+        idx, tt = mod.hard_spec()
+        oidx, ott = OH.fc_hard_spec(L)
+        np.testing.assert_array_equal(idx.numpy(), oidx)
+        P = ott.shape[1]
+        bits = ((tt.unsqueeze(1) >> torch.arange(P)) & 1).bool().numpy()
+        np.testing.assert_array_equal(bits, ott)
+    if spec["type"] == "conv":
+        for Bk, conv in zip(spec["blocks"], m.blocks[0::2]):
+            leaf, tt = conv.hard_spec()
+            oleaf, otts = OH.conv_hard_spec(Bk)
+            np.testing.assert_array_equal(leaf.numpy(), oleaf)
+            ott = np.concatenate(otts, axis=1)            # [n, total, P]
+            P = ott.shape[2]
+            bits = ((tt.unsqueeze(-1) >> torch.arange(P)) & 1).bool().numpy()
+            np.testing.assert_array_equal(bits, ott)
+
+
+def test_gate16_lut_codes():
+    from silogic_b200.functional import gate16_lut_codes, TRUTH_TABLES
+    codes = gate16_lut_codes()
+    for g in range(16):
+        for a in (0, 1):
+            for b in (0, 1):
+                assert ((int(codes[g]) >> (a | (b << 1))) & 1) == int(TRUTH_TABLES[g, (a << 1) | b])
+
+
+def test_ldw_and_words():
+    assert [_hard.n_words(b) for b in (1, 64, 65, 128, 129)] == [1, 1, 2, 2, 3]
+    assert _hard.ldw_for(1) == 2 and _hard.ldw_for(129) == 4 and _hard.ldw_for(256) == 4
+
+
+def test_cpu_tensors_are_rejected():
+    import silogic_b200 as S
+    net = S.LogicNet(16, 20, 2)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        net.forward_hard(torch.zeros(4, 16))
