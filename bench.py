@@ -218,6 +218,57 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
                 fc_bytes=(width + width) * nw * 8)
 
 
+# ------------------------------------------------------------------ soft leg
+def soft_bytes_per_sample(cfg):
+    """Layer-wise algorithmic fp32 bytes per sample of soft fwd+bwd (each stage reads its
+    inputs once and writes its outputs once; the data input needs no gradient)."""
+    kw = cfg["kwargs"]
+    dims = [kw["in_dim"]] + [kw["width"]] * kw["depth"]
+    fwd = sum((a + b) * 4 for a, b in zip(dims[:-1], dims[1:]))
+    bwd = sum((b + a + (a if i > 0 else 0)) * 4 for i, (a, b) in enumerate(zip(dims[:-1], dims[1:])))
+    W = dims[-1]
+    return fwd + bwd + (4 * W + 40) * 2
+
+
+def run_soft(cfg, B, steps, warmup, rank, ws, dev):
+    model = build_model(cfg).to(dev).train()
+    x = make_input(cfg, B, seed=100 + rank).float().to(dev)
+    g = torch.Generator().manual_seed(5)
+    rmat = torch.randn(B, 10, generator=g).to(dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.int32, device=dev)
+    params = [p for p in model.parameters()]
+    bucket = None
+
+    def step():
+        nonlocal bucket
+        for p in params:
+            p.grad = None
+        logits = model(x)
+        (logits * rmat).sum().backward()
+        if ws > 1:      # data parallel: one all-reduce of every parameter gradient
+            bucket = torch.cat([p.grad.reshape(-1) for p in params])
+            torch.distributed.all_reduce(bucket)
+        return logits
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    times = []
+    for _ in range(steps):
+        flush.fill_(1)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        times.append((e0, e1))
+    torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in times)
+    return dict(ms=ms)
+
+
 # ------------------------------------------------------------ CPU baselines
 _SPEC_CACHE = {}
 
@@ -252,6 +303,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--cpu-sample", type=int, default=4096)
+    ap.add_argument("--no-soft", action="store_true")
     a = ap.parse_args()
     cfg = CONFIGS[a.config]
     ws, rank, local = dist_env()
@@ -287,10 +339,13 @@ def main():
     dev = torch.device("cuda", local)
     B = cfg["hard_batch"]
     r = run_hard(cfg, B, a.steps, warmup, rank, ws, dev)
-    ms = torch.tensor([r["ms"], r["e2e_ms"]], device=dev)
+    soft = None
+    if not a.no_soft:
+        soft = run_soft(cfg, cfg["soft_batch"], a.steps, warmup, rank, ws, dev)
+    ms = torch.tensor([r["ms"], r["e2e_ms"], soft["ms"] if soft else 0.0], device=dev)
     if ws > 1:
         torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
-    ms_step, e2e_ms = ms.tolist()
+    ms_step, e2e_ms, soft_ms = ms.tolist()
     hbm, kind = peaks()
     fc_gbs = r["fc_bytes"] / (r["fc_ms"] * 1e-3) / 1e9
     if rank == 0:
@@ -310,6 +365,17 @@ def main():
                          "algorithmic_bytes_per_launch": r["fc_bytes"]},
             "clocks": r["clocks"],
         }
+        if soft:
+            Bs = cfg["soft_batch"]
+            bps = soft_bytes_per_sample(cfg)
+            ach = bps * Bs / (soft_ms * 1e-3) / 1e9
+            line["soft_fwd_bwd"] = {
+                "metric": "soft fwd+bwd samples/s", "value": Bs * ws / (soft_ms * 1e-3),
+                "unit": "samples/s", "ms_per_step": soft_ms, "batch_per_gpu": Bs, "dtype": "f32",
+                "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                             "frac": ach / hbm, "algorithmic_bytes_per_sample": bps,
+                             "scope": "whole step (layer-wise bytes)"},
+                "collective": "one NCCL all-reduce of all parameter gradients" if ws > 1 else None}
         if ws == 1:
             v, dt = cpu_hard_sample(cfg, a.cpu_sample, 1)
             line["cpu_baseline"] = {"value": v, "unit": "samples/s", "cores": 1, "kind": "port",

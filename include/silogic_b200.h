@@ -103,6 +103,82 @@ int slg_conv_hard(const uint64_t* x, int64_t cin, int64_t H, int64_t W, int64_t 
 int slg_groupsum(const uint64_t* x, int64_t width, int64_t ldw, int64_t B,
                  int32_t num_classes, int32_t* counts, void* stream);
 
+/* ------------------------------------------------------- soft FC layer */
+
+/* Node kinds of the soft kernels. */
+#define SLG_NODE_GATE16 0      /* 16-gate softmax mixture, BasisProj form (arity 2)  */
+#define SLG_NODE_WALSH 1       /* sigmoid(sum_M theta_M prod (2a-1) * inv_tau)         */
+#define SLG_NODE_MULTILINEAR 2 /* multilinear interpolation of sigmoid(logits)         */
+#define SLG_NODE_HYBRID 3      /* discrete forward, multilinear surrogate gradient     */
+#define SLG_NODE_LINEAR 4      /* sigmoid(theta_0 + sum_j theta_j a_j)                 */
+
+/* Soft forward of one FC logic layer on feature-major x [in_dim, ldb]:
+ *   a_j[o,b] = sum_k w[o,j,k] x[cand[o,j,k], b],  w = softmax_k(conn[o,j,:])
+ *              (one-hot argmax when conn_ste; w = 1 with K = 1 when conn == NULL)
+ *   y[o,b]   = node(a[o,:,b]) with raw node parameters params[o, :]
+ *              (gate16: 16 gate logits, softmax, or argmax one-hot when gate_hard;
+ *               walsh: 2^arity theta; multilinear/hybrid: 2^arity logits; linear: arity+1)
+ *   rows o < wire_r copy x[o] (wire residual).
+ * K <= 16, arity 1..6 (gate16: 2).  Replaces dense_logic / warp_logic /
+ * multilinear_logic (silogic/kernels/dense.py:91-125, warp.py:79-105,
+ * multilinear.py:130-176) and the PyTorch path of LogicLayer.forward
+ * (silogic/layers.py:125-129), with the connectome softmax and the node's
+ * parameter transform (gate_probs @ basis, sigmoid) fused in. */
+int slg_fc_soft_fwd(const float* x, int64_t in_dim, int64_t ldb, const int32_t* cand,
+                    const float* conn, int32_t K, int32_t conn_ste, int32_t node, int32_t arity,
+                    const float* params, int32_t gate_hard, float inv_tau, int64_t out_dim,
+                    int64_t wire_r, float* y, void* stream);
+
+/* Bytes of scratch slg_fc_soft_bwd needs (per-chunk parameter-gradient partials). */
+int64_t slg_fc_soft_workspace_bytes(int64_t ldb, int32_t K, int32_t node, int32_t arity,
+                                    int64_t out_dim);
+
+/* Backward of slg_fc_soft_fwd (same arguments) given gy [out_dim, ldb]:
+ *   gx [in_dim, ldb] += dL/dx (atomic float4 adds; caller zero-fills; NULL = skip),
+ *   gconn [out_dim, arity, K] = dL/dconn (softmax Jacobian; STE uses the soft one),
+ *   gparams [out_dim, P] = dL/dparams.  Padding columns of gy must be zero.
+ * Replaces DenseLogicFn/WarpFn/MultilinearLogicFn.backward (dense.py:108-120,
+ * warp.py:91-101, multilinear.py:147-159) plus the torch autograd of the
+ * connectome softmax and gate_probs. */
+int slg_fc_soft_bwd(const float* x, int64_t in_dim, int64_t ldb, const int32_t* cand,
+                    const float* conn, int32_t K, int32_t conn_ste, int32_t node, int32_t arity,
+                    const float* params, int32_t gate_hard, float inv_tau, int64_t out_dim,
+                    int64_t wire_r, const float* gy, float* gx, float* gconn, float* gparams,
+                    void* workspace, int64_t workspace_bytes, void* stream);
+
+/* -------------------------------------------------- soft-path boundaries */
+
+/* [B, F] sample-major -> [F, ldb] feature-major (columns >= B zeroed), and back. */
+int slg_to_feature_major(const float* x, int64_t B, int64_t F, float* out, int64_t ldb,
+                         void* stream);
+int slg_from_feature_major(const float* xt, int64_t F, int64_t ldb, int64_t B, float* out,
+                           void* stream);
+
+/* Soft GroupSum on feature-major x [width, ldb] -> logits [B, C]:
+ * sum over each class block of (x > 0.5) (feature_ste) or x, divided by tau
+ * (silogic/heads.py:34-39).  Backward: gx[f, b] = glogits[b, f / G] / tau. */
+int slg_groupsum_soft_fwd(const float* x, int64_t width, int64_t ldb, int64_t B,
+                          int32_t num_classes, float tau, int32_t feature_ste, float* logits,
+                          void* stream);
+int slg_groupsum_soft_bwd(const float* glogits, int64_t width, int64_t ldb, int64_t B,
+                          int32_t num_classes, float tau, float* gx, void* stream);
+
+/* OrPool on N = B*C planes of H x W (silogic/layers.py:548-563): max over
+ * size x size windows; backward routes to the first maximum (row-major, strict >),
+ * accumulating into gx (caller zero-fills). */
+int slg_or_pool_fwd(const float* x, int64_t N, int64_t H, int64_t W, int32_t size, float* y,
+                    void* stream);
+int slg_or_pool_bwd(const float* x, const float* gy, int64_t N, int64_t H, int64_t W,
+                    int32_t size, float* gx, void* stream);
+
+/* LearnedThermometerEncoder.forward (silogic/encoders.py:39-44): out[b, f*T+t] =
+ * (x[b,f] - thr[f,t] > 0); backward uses the sigmoid(scale*d) straight-through
+ * gradient, accumulating into gx [B, F] (may be NULL) and gthr [F, T] (zero-filled). */
+int slg_thermo_soft_fwd(const float* x, const float* thr, int64_t B, int64_t F, int32_t T,
+                        float* out, void* stream);
+int slg_thermo_soft_bwd(const float* x, const float* thr, const float* g, int64_t B, int64_t F,
+                        int32_t T, float scale, float* gx, float* gthr, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -28,7 +28,21 @@ _SIGS = {
     "slg_conv_hard": [_p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _i64, _i64,
                       _i32, _p, _p],
     "slg_groupsum": [_p, _i64, _i64, _i64, _i32, _p, _p],
+    "slg_fc_soft_fwd": [_p, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _p, _i32, _f32, _i64,
+                        _i64, _p, _p],
+    "slg_fc_soft_bwd": [_p, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _p, _i32, _f32, _i64,
+                        _i64, _p, _p, _p, _p, _p, _i64, _p],
+    "slg_to_feature_major": [_p, _i64, _i64, _p, _i64, _p],
+    "slg_from_feature_major": [_p, _i64, _i64, _i64, _p, _p],
+    "slg_groupsum_soft_fwd": [_p, _i64, _i64, _i64, _i32, _f32, _i32, _p, _p],
+    "slg_groupsum_soft_bwd": [_p, _i64, _i64, _i64, _i32, _f32, _p, _p],
+    "slg_or_pool_fwd": [_p, _i64, _i64, _i64, _i32, _p, _p],
+    "slg_or_pool_bwd": [_p, _p, _i64, _i64, _i64, _i32, _p, _p],
+    "slg_thermo_soft_fwd": [_p, _p, _i64, _i64, _i32, _p, _p],
+    "slg_thermo_soft_bwd": [_p, _p, _p, _i64, _i64, _i32, _f32, _p, _p, _p],
 }
+# entry points that do not return a status
+_RESTYPES = {"slg_fc_soft_workspace_bytes": ([_i64, _i32, _i32, _i32, _i64], ctypes.c_int64)}
 
 _lib = None
 
@@ -50,6 +64,10 @@ def lib():
             fn = getattr(L, name)
             fn.argtypes = args
             fn.restype = ctypes.c_int
+        for name, (args, res) in _RESTYPES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
         L.slg_last_error.restype = ctypes.c_char_p
         L.slg_last_error.argtypes = []
         _lib = L

@@ -1,33 +1,314 @@
-"""Soft (relaxed, differentiable) ops -- host side of the fp32 CUDA kernels."""
+"""Soft (relaxed, fp32) path: autograd Functions around the CUDA kernels.
+
+Inside a network the activations are feature-major ``[F, ldb]`` (``ldb`` = batch
+rounded up to a multiple of 4, padding columns zero) so each connectome gather
+reads whole rows; the module boundary transposes once with a CUDA kernel.
+Every Function's backward is a CUDA kernel too; parameter-side transforms
+(connection softmax, gate_probs @ basis, sigmoid of LUT logits) are fused into
+the layer kernels.
+"""
 import torch
 
 from . import _hard
+from ._lib import call, lib, ptr, require_cuda, stream_ptr
+
+NODE_ID = {"gate16": 0, "walsh": 1, "multilinear": 2, "hybrid": 3, "linear": 4}
 
 
-def _todo(*a, **k):
-    raise NotImplementedError("soft kernels are not built yet")
+def ldb_for(B):
+    return max(4, (int(B) + 3) // 4 * 4)
 
 
-fc_supported = lambda layer: True
-logic_layer_forward = _todo
-node_forward = _todo
-conv_tree_forward = _todo
-group_sum_forward = _todo
-logic_net_features = _todo
-logic_net_logits = _todo
-logic_conv_net_features = _todo
-logic_conv_net_logits = _todo
-thermometer_forward = _todo
-or_pool = _todo
+# ------------------------------------------------------------- transposes
+class ToFeatureMajor(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x):
+        require_cuda(x)
+        B = x.shape[0]
+        x2 = x.reshape(B, -1).float().contiguous()
+        F = x2.shape[1]
+        ldb = ldb_for(B)
+        out = torch.empty((F, ldb), dtype=torch.float32, device=x.device)
+        call("slg_to_feature_major", ptr(x2), B, F, ptr(out), ldb, stream_ptr(x.device))
+        ctx.shape = x.shape
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        B = ctx.shape[0]
+        g = g.contiguous()
+        F, ldb = g.shape
+        out = torch.empty((B, F), dtype=torch.float32, device=g.device)
+        call("slg_from_feature_major", ptr(g), F, ldb, B, ptr(out), stream_ptr(g.device))
+        return out.view(ctx.shape)
+
+
+class FromFeatureMajor(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, xt, B):
+        xt = xt.contiguous()
+        F, ldb = xt.shape
+        out = torch.empty((B, F), dtype=torch.float32, device=xt.device)
+        call("slg_from_feature_major", ptr(xt), F, ldb, B, ptr(out), stream_ptr(xt.device))
+        ctx.ldb = ldb
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        g = g.float().contiguous()
+        B, F = g.shape
+        out = torch.empty((F, ctx.ldb), dtype=torch.float32, device=g.device)
+        call("slg_to_feature_major", ptr(g), B, F, ptr(out), ctx.ldb, stream_ptr(g.device))
+        return out, None
+
+
+# --------------------------------------------------------------- FC layer
+def fc_supported(layer):
+    from .connectomes import FixedConnectome, TopKConnectome
+    if layer.node.kind not in NODE_ID:
+        return False
+    if not isinstance(layer._conn, (FixedConnectome, TopKConnectome)):
+        return False
+    if isinstance(layer._conn, TopKConnectome) and layer._conn.k > 16:
+        return False
+    if layer.node.kind == "walsh" and layer.node.gate_select == "gumbel" and layer.training:
+        return False
+    return 1 <= layer.arity <= 6
+
+
+def _fc_meta(layer, wire_r=0):
+    """Static launch description of a LogicLayer's soft kernel."""
+    from .connectomes import FixedConnectome, TopKConnectome
+    if not fc_supported(layer):
+        raise NotImplementedError(
+            f"no soft kernel for node={layer.node.kind!r} connectome={type(layer._conn).__name__} "
+            f"arity={layer.arity} in silogic_b200")
+    node = layer.node
+    kind = node.kind
+    if isinstance(layer._conn, FixedConnectome):
+        cand, K, ste, conn = layer._conn.cand_i32, 1, 0, None
+    else:
+        cand, K, ste, conn = layer._conn.cand_i32, layer._conn.k, int(layer._conn.ste), layer._conn.conn
+    gate_hard = 0
+    params = node.param
+    if kind == "gate16" and layer.training:
+        if node.gate_select == "hard":
+            gate_hard = 1
+        elif node.gate_select == "gumbel":
+            g = -torch.empty_like(params).exponential_().log()
+            params = (params + g) / node.gumbel_tau
+            gate_hard = 1
+    inv_tau = float(node.inv_tau) if kind == "walsh" else 1.0
+    return dict(cand=cand.contiguous(), K=K, ste=ste, node=NODE_ID[kind], arity=layer.arity,
+                gate_hard=gate_hard, inv_tau=inv_tau, out_dim=layer.out_dim,
+                wire_r=wire_r), params, conn
+
+
+class FCSoft(torch.autograd.Function):
+    """Feature-major soft FC layer: xt [in, ldb] -> yt [out, ldb]."""
+
+    @staticmethod
+    def forward(ctx, xt, params, conn, meta):
+        require_cuda(xt)
+        xt = xt.contiguous()
+        params = params.float().contiguous()
+        connc = conn.float().contiguous() if conn is not None else None
+        in_dim, ldb = xt.shape
+        y = torch.empty((meta["out_dim"], ldb), dtype=torch.float32, device=xt.device)
+        call("slg_fc_soft_fwd", ptr(xt), in_dim, ldb, ptr(meta["cand"]), ptr(connc), meta["K"],
+             meta["ste"], meta["node"], meta["arity"], ptr(params), meta["gate_hard"],
+             meta["inv_tau"], meta["out_dim"], meta["wire_r"], ptr(y), stream_ptr(xt.device))
+        ctx.save_for_backward(xt, params, connc)
+        ctx.meta = meta
+        ctx.has_conn = conn is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        xt, params, connc = ctx.saved_tensors
+        m = ctx.meta
+        gy = gy.contiguous()
+        in_dim, ldb = xt.shape
+        gx = torch.zeros_like(xt) if ctx.needs_input_grad[0] else None
+        gparams = torch.empty_like(params)
+        gconn = torch.empty_like(connc) if connc is not None else None
+        nbytes = lib().slg_fc_soft_workspace_bytes(ldb, m["K"], m["node"], m["arity"], m["out_dim"])
+        ws = torch.empty(max(nbytes, 4) // 4 + 1, dtype=torch.float32, device=xt.device)
+        call("slg_fc_soft_bwd", ptr(xt), in_dim, ldb, ptr(m["cand"]), ptr(connc), m["K"], m["ste"],
+             m["node"], m["arity"], ptr(params), m["gate_hard"], m["inv_tau"], m["out_dim"],
+             m["wire_r"], ptr(gy), ptr(gx), ptr(gconn), ptr(gparams), ptr(ws), ws.numel() * 4,
+             stream_ptr(xt.device))
+        return gx, gparams, gconn, None
+
+
+def fc_layer_fm(layer, xt, wire_r=0):
+    meta, params, conn = _fc_meta(layer, wire_r)
+    return FCSoft.apply(xt, params, conn, meta)
+
+
+def logic_layer_forward(layer, x):
+    """``LogicLayer.forward`` on ``[B, in]``."""
+    require_cuda(x)
+    B = x.shape[0]
+    return FromFeatureMajor.apply(fc_layer_fm(layer, ToFeatureMajor.apply(x)), B)
+
+
+def node_forward(node, x, idx):
+    """``Node.forward`` on operands flattened to ``[B, out*arity]`` (identity wiring)."""
+    from types import SimpleNamespace
+    from .connectomes import FixedConnectome
+    conn = FixedConnectome.__new__(FixedConnectome)
+    torch.nn.Module.__init__(conn)
+    conn.cand_i32 = idx.unsqueeze(-1).contiguous()
+    fake = SimpleNamespace(node=node, _conn=conn, arity=node.arity, out_dim=node.out_dim,
+                           training=node.training)
+    meta, params, c = _fc_meta(fake)
+    B = x.shape[0]
+    return FromFeatureMajor.apply(FCSoft.apply(ToFeatureMajor.apply(x), params, c, meta), B)
+
+
+# ---------------------------------------------------------------- GroupSum
+class GroupSumSoft(torch.autograd.Function):
+    """Feature-major GroupSum: xt [W, ldb] -> logits [B, C]."""
+
+    @staticmethod
+    def forward(ctx, xt, B, C, tau, ste):
+        xt = xt.contiguous()
+        W, ldb = xt.shape
+        out = torch.empty((B, C), dtype=torch.float32, device=xt.device)
+        call("slg_groupsum_soft_fwd", ptr(xt), W, ldb, B, C, float(tau), int(ste), ptr(out),
+             stream_ptr(xt.device))
+        ctx.dims = (W, ldb, B, C, float(tau))
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        W, ldb, B, C, tau = ctx.dims
+        g = g.float().contiguous()
+        gx = torch.empty((W, ldb), dtype=torch.float32, device=g.device)
+        call("slg_groupsum_soft_bwd", ptr(g), W, ldb, B, C, tau, ptr(gx), stream_ptr(g.device))
+        return gx, None, None, None, None
+
+
+def group_sum_forward(x, num_classes, tau, feature_ste):
+    """``GroupSum.forward`` on ``[B, W]``."""
+    require_cuda(x)
+    B = x.shape[0]
+    return GroupSumSoft.apply(ToFeatureMajor.apply(x), B, num_classes, tau, feature_ste)
+
+
+# ----------------------------------------------------------------- networks
+def logic_net_features_fm(net, x):
+    B = x.shape[0]
+    xt = ToFeatureMajor.apply(x)
+    for layer in net.layers:
+        wr = net.wire_r if (net.wire_r and layer.in_dim == layer.out_dim) else 0
+        xt = fc_layer_fm(layer, xt, wr)
+    return xt, B
+
+
+def logic_net_features(net, x):
+    require_cuda(x)
+    xt, B = logic_net_features_fm(net, x)
+    return FromFeatureMajor.apply(xt, B)
+
+
+def logic_net_logits(net, x):
+    require_cuda(x)
+    xt, B = logic_net_features_fm(net, x)
+    h = net.head
+    return GroupSumSoft.apply(xt, B, h.num_classes, h.tau, h.feature_ste)
+
+
+def logic_conv_net_features_fm(net, x):
+    raise NotImplementedError("soft conv kernels are not built yet")
+
+
+def logic_conv_net_features(net, x):
+    require_cuda(x)
+    xt, B = logic_conv_net_features_fm(net, x)
+    return FromFeatureMajor.apply(xt, B)
+
+
+def logic_conv_net_logits(net, x):
+    require_cuda(x)
+    xt, B = logic_conv_net_features_fm(net, x)
+    h = net.head
+    return GroupSumSoft.apply(xt, B, h.num_classes, h.tau, h.feature_ste)
+
+
+def conv_tree_forward(conv, x, pool=1):
+    raise NotImplementedError("soft conv kernels are not built yet")
+
+
+# ------------------------------------------------------------------ OrPool
+class OrPoolSoft(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, size):
+        x = x.float().contiguous()
+        B, C, H, W = x.shape
+        y = torch.empty((B, C, H // size, W // size), dtype=torch.float32, device=x.device)
+        call("slg_or_pool_fwd", ptr(x), B * C, H, W, size, ptr(y), stream_ptr(x.device))
+        ctx.save_for_backward(x)
+        ctx.size = size
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        (x,) = ctx.saved_tensors
+        B, C, H, W = x.shape
+        gy = gy.contiguous()
+        gx = torch.zeros_like(x)
+        call("slg_or_pool_bwd", ptr(x), ptr(gy), B * C, H, W, ctx.size, ptr(gx), stream_ptr(x.device))
+        return gx, None
+
+
+def or_pool(x, size):
+    require_cuda(x)
+    return OrPoolSoft.apply(x, size)
 
 
 @torch.no_grad()
 def or_pool_hard(x, size):
-    raise NotImplementedError
+    require_cuda(x)
+    return OrPoolSoft.apply(x.float(), size).to(torch.uint8)
+
+
+# -------------------------------------------------------------- encoder
+class ThermometerSoft(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, thr, scale):
+        x = x.float().contiguous()
+        thr = thr.float().contiguous()
+        B, F = x.shape
+        T = thr.shape[1]
+        out = torch.empty((B, F * T), dtype=torch.float32, device=x.device)
+        call("slg_thermo_soft_fwd", ptr(x), ptr(thr), B, F, T, ptr(out), stream_ptr(x.device))
+        ctx.save_for_backward(x, thr)
+        ctx.scale = float(scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        x, thr = ctx.saved_tensors
+        B, F = x.shape
+        T = thr.shape[1]
+        g = g.float().contiguous()
+        gx = torch.zeros_like(x) if ctx.needs_input_grad[0] else None
+        gthr = torch.zeros_like(thr)
+        call("slg_thermo_soft_bwd", ptr(x), ptr(thr), ptr(g), B, F, T, ctx.scale, ptr(gx),
+             ptr(gthr), stream_ptr(x.device))
+        return gx, gthr, None
+
+
+def thermometer_forward(x, thresholds, scale):
+    require_cuda(x)
+    return ThermometerSoft.apply(x, thresholds, scale)
 
 
 @torch.no_grad()
 def thermometer_hard(x, thresholds):
+    require_cuda(x)
     B, F = x.shape
     T = thresholds.shape[1]
     h = _hard.thermo_pack(x.view(B, F, 1, 1), thresholds, mode=1)   # [F*T, 1, 1, ldw]

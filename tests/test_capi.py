@@ -14,7 +14,7 @@ HEADER = os.path.join(ROOT, "include", "silogic_b200.h")
 
 def _declared():
     src = open(HEADER).read()
-    return sorted(set(re.findall(r"\b(?:int|const char\*)\s+(slg_\w+)\s*\(", src)))
+    return sorted(set(re.findall(r"\b(?:int|int64_t|const char\*)\s+(slg_\w+)\s*\(", src)))
 
 
 @pytest.fixture(scope="module")

@@ -1,0 +1,171 @@
+"""Soft forward + backward on the GPU vs the reference golden vectors and the
+torch-fp32 oracle.
+
+Tolerances: activations |got - ref| <= 1e-5 |ref| + 1e-6; gradients norm-wise
+|got - ref| <= 1e-5 (|ref| + max|ref|) + 1e-7 (fp32, summation order differs);
+GroupSum logits exact except where a feature lies within 1e-5 of the 0.5
+threshold (a 1-ulp difference there flips a count by design of feature_ste).
+"""
+import numpy as np
+import pytest
+import torch
+
+from helpers import FIXTURES, build_model, encoder_image
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+FC = [n for n in FIXTURES if n.startswith("fc_")]
+CONV = [n for n in FIXTURES if n.startswith("conv_")]
+
+
+def assert_grad_close(got, ref, what):
+    got = got.detach().cpu().numpy() if torch.is_tensor(got) else got
+    tol = 1e-5 * (np.abs(ref) + np.abs(ref).max()) + 1e-7
+    bad = np.abs(got - ref) > tol
+    assert not bad.any(), f"{what}: {bad.sum()} of {bad.size} entries off, max err " \
+                          f"{np.abs(got - ref).max():.3e} (ref max {np.abs(ref).max():.3e})"
+
+
+def assert_logits_close(logits, ref, feat_ref, tau):
+    d = np.abs(logits - ref) * tau                        # in counts
+    near = (np.abs(feat_ref - 0.5) <= 1e-5).sum(1)[:, None]   # per sample
+    assert np.all(d <= near + 1e-3), f"logit counts differ beyond threshold ties: {d.max()}"
+
+
+def run_soft(name):
+    m, enc, z, _ = build_model(name, dev)
+    m.train()
+    x = torch.from_numpy(z["x"]).to(dev).requires_grad_(True)
+    xs = x
+    if enc is not None:
+        xs = encoder_image(enc(x), z)
+    feat = m._run(xs, hard=False)
+    logits = m(xs)
+    (logits * torch.from_numpy(z["rmat"]).to(dev)).sum().backward()
+    return m, enc, z, x, feat, logits
+
+
+@pytest.mark.parametrize("name", FC)
+def test_fc_soft_matches_reference_golden(name):
+    m, enc, z, x, feat, logits = run_soft(name)
+    np.testing.assert_allclose(feat.detach().cpu().numpy(), z["feat"], rtol=1e-5, atol=1e-6)
+    assert_logits_close(logits.detach().cpu().numpy(), z["logits"], z["feat"], m.head.tau)
+    params = dict(m.named_parameters())
+    for k in z.files:
+        if k.startswith("grad/"):
+            n = k[5:]
+            got = x.grad if n == "x" else params[n].grad
+            assert got is not None, n
+            assert_grad_close(got, z[k], f"{name} grad {n}")
+
+
+def _rand_model(ctor, kw, seed):
+    import silogic_b200 as S
+    torch.manual_seed(seed)
+    m = getattr(S, ctor)(**kw)
+    g = torch.Generator().manual_seed(seed + 1)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.copy_(torch.randn(p.shape, generator=g))
+    return m
+
+
+def oracle_soft(ctor, kw, m, x, rmat):
+    from oracle import soft as OS
+    from oracle.spec import net_spec
+    sd = {k: v.detach().cpu() for k, v in m.state_dict().items()}
+    spec = net_spec(ctor, kw, {k: v.numpy() for k, v in sd.items()})
+    P = OS.params_from_sd(sd)
+    xr = x.detach().cpu().clone().requires_grad_(True)
+    feat = OS.net_features(spec, P, xr, training=True)
+    logits = OS.group_sum(feat, spec["num_classes"], spec["tau"])
+    (logits * rmat).sum().backward()
+    return feat.detach().numpy(), logits.detach().numpy(), P, xr.grad
+
+
+@pytest.mark.parametrize("kw", [
+    dict(in_dim=784, width=2000, depth=3, node="walsh", connectome="topk", k=8, tau=10.0, seed=0),
+    dict(in_dim=784, width=1600, depth=2, node="gate16", connectome="fixed", tau=10.0, seed=1),
+    dict(in_dim=300, width=1000, depth=2, node="gate16", connectome="topk", k=16, tau=3.0, seed=2),
+    dict(in_dim=300, width=500, depth=2, node="multilinear", arity=6, connectome="topk", k=2,
+         tau=5.0, seed=3),
+    dict(in_dim=300, width=500, depth=2, node="linear", arity=3, connectome="topk", k=4, tau=5.0,
+         seed=4),
+], ids=["walsh_topk8", "gate16_fixed", "gate16_topk16", "multilinear6", "linear3"])
+@pytest.mark.parametrize("B", [1, 515])
+def test_fc_soft_vs_oracle(kw, B):
+    m = _rand_model("LogicNet", kw, 11)
+    g = torch.Generator().manual_seed(B)
+    x = (torch.rand(B, kw["in_dim"], generator=g) < 0.3).float()
+    rmat = torch.randn(B, 10, generator=g)
+    f_ref, l_ref, P, gx_ref = oracle_soft("LogicNet", kw, m, x, rmat)
+    m = m.to(dev).train()
+    xd = x.to(dev).requires_grad_(True)
+    feat = m._run(xd, hard=False)
+    np.testing.assert_allclose(feat.detach().cpu().numpy(), f_ref, rtol=1e-5, atol=1e-6)
+    logits = m(xd)
+    assert_logits_close(logits.detach().cpu().numpy(), l_ref, f_ref, m.head.tau)
+    (logits * rmat.to(dev)).sum().backward()
+    assert_grad_close(xd.grad, gx_ref.numpy(), "x")
+    for n, p in m.named_parameters():
+        assert_grad_close(p.grad, P[n].grad.numpy(), n)
+
+
+def test_layer_and_node_level_soft_vs_torch_math():
+    """LogicLayer.forward / Node.forward on [B, in] match the reference formulas."""
+    import silogic_b200 as S
+    torch.manual_seed(0)
+    layer = S.LogicLayer(64, 96, node="walsh", connectome="topk", k=4, seed=3).to(dev)
+    x = torch.rand(37, 64, device=dev)
+    y = layer(x)
+    w = torch.softmax(layer._conn.conn, 2)
+    ops = torch.einsum("boak,oak->boa", x[:, layer._conn.cand], w)
+    u = 2 * ops - 1
+    t = layer.node.theta
+    z = t[:, 0] + t[:, 1] * u[..., 0] + t[:, 2] * u[..., 1] + t[:, 3] * u[..., 0] * u[..., 1]
+    torch.testing.assert_close(y, torch.sigmoid(z), rtol=1e-5, atol=1e-6)
+    node = S.build_node("multilinear", 20, arity=3).to(dev)
+    opnd = torch.rand(9, 20, 3, device=dev)
+    c = node.corners
+    ref = ((c * opnd.unsqueeze(2) + (1 - c) * (1 - opnd.unsqueeze(2))).prod(3)
+           * torch.sigmoid(node.logits)[None]).sum(2)
+    torch.testing.assert_close(node(opnd), ref, rtol=1e-5, atol=1e-6)
+
+
+def test_groupsum_orpool_thermometer_soft():
+    import silogic_b200 as S
+    x = torch.rand(33, 50, device=dev, requires_grad=True)
+    gs = S.GroupSum(5, tau=2.0, feature_ste=True)
+    y = gs(x)
+    ref = (x > 0.5).float().view(33, 5, 10).sum(2) / 2.0
+    torch.testing.assert_close(y, ref)
+    y.sum().backward()
+    torch.testing.assert_close(x.grad, torch.full_like(x, 0.5))
+    # OrPool: max with first-max gradient routing (ties are common on binary inputs)
+    xi = (torch.rand(3, 4, 7, 6, device=dev) < 0.5).float().requires_grad_(True)
+    xr = xi.detach().clone().requires_grad_(True)
+    p = S.OrPool(2)
+    yi = p(xi)
+    yr = torch.nn.functional.max_pool2d(xr.cpu(), 2, 2)
+    torch.testing.assert_close(yi.cpu(), yr)
+    g = torch.randn_like(yi)
+    yi.backward(g)
+    xc = xr.detach().cpu().requires_grad_(True)
+    torch.nn.functional.max_pool2d(xc, 2, 2).backward(g.cpu())
+    torch.testing.assert_close(xi.grad.cpu(), xc.grad)
+    # learned thermometer
+    from oracle import soft as OS
+    enc = S.LearnedThermometerEncoder(40, 3).to(dev)
+    with torch.no_grad():
+        enc.thresholds.copy_(torch.rand(40, 3))
+    xe = torch.rand(21, 40, device=dev, requires_grad=True)
+    out = enc(xe)
+    thr = enc.thresholds.detach().cpu().clone().requires_grad_(True)
+    xc = xe.detach().cpu().clone().requires_grad_(True)
+    ref = OS.learned_thermometer(xc, thr)
+    torch.testing.assert_close(out.cpu(), ref, rtol=0, atol=1e-6)
+    gg = torch.randn_like(out)
+    out.backward(gg)
+    ref.backward(gg.cpu())
+    assert_grad_close(xe.grad, xc.grad.numpy(), "enc x")
+    assert_grad_close(enc.thresholds.grad, thr.grad.numpy(), "enc thr")
