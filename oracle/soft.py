@@ -141,8 +141,19 @@ def group_sum(x, num_classes, tau):
     return x.view(B, num_classes, Wd // num_classes).sum(dim=2) / tau
 
 
-def net_features(spec, P, x, training=True):
-    """``model._run(x, hard=False)``: activations entering the head."""
+def _pool_at(y, idx):
+    """2x2 pooling that takes the value at given flat window indices (into H*W)."""
+    B, n, H, W = y.shape
+    return y.reshape(B, n, H * W).gather(2, idx.reshape(B, n, -1)).view(idx.shape)
+
+
+def net_features(spec, P, x, training=True, pool_index=None):
+    """``model._run(x, hard=False)``: activations entering the head.
+
+    ``pool_index`` (optional, one LongTensor ``[B, n, Hp, Wp]`` per block) fixes
+    which window element each OR-pool output takes; by default the routing is
+    ``F.max_pool2d``'s.  Tests use it to replay another implementation's choice
+    at windows whose values tie to within fp32 rounding."""
     if spec["type"] == "fc":
         for L in spec["layers"]:
             y = fc_layer(L, P, x, training)
@@ -156,7 +167,10 @@ def net_features(spec, P, x, training=True):
             r = min(int(Bk["n"] * spec["wire_residual"]), x.shape[1])
             if r > 0:
                 y = torch.cat([x[:, :r], y[:, r:]], dim=1)
-        x = F.max_pool2d(y, 2, 2)                                 # layers.py:558-559
+        if pool_index is None:
+            x = F.max_pool2d(y, 2, 2)                             # layers.py:558-559
+        else:
+            x = _pool_at(y, pool_index[spec["blocks"].index(Bk)])
     x = x.flatten(1)
     for L in spec["head"]:
         x = fc_layer(L, P, x, training)

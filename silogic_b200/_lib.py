@@ -40,9 +40,17 @@ _SIGS = {
     "slg_or_pool_bwd": [_p, _p, _i64, _i64, _i64, _i32, _p, _p],
     "slg_thermo_soft_fwd": [_p, _p, _i64, _i64, _i32, _p, _p],
     "slg_thermo_soft_bwd": [_p, _p, _p, _i64, _i64, _i32, _f32, _p, _p, _p],
+    "slg_conv_soft_fwd": [_p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _i32, _p,
+                          _i32, _f32, _i32, _i32, _i64, _i64, _i32, _p, _p],
+    "slg_conv_soft_bwd": [_p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _i32, _p,
+                          _i32, _f32, _i32, _i32, _i64, _i64, _i32, _p, _p, _p, _p, _p, _i64, _p],
 }
 # entry points that do not return a status
-_RESTYPES = {"slg_fc_soft_workspace_bytes": ([_i64, _i32, _i32, _i32, _i64], ctypes.c_int64)}
+_RESTYPES = {
+    "slg_fc_soft_workspace_bytes": ([_i64, _i32, _i32, _i32, _i64], ctypes.c_int64),
+    "slg_conv_soft_workspace_bytes": ([_i64, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+                                       _i64], ctypes.c_int64),
+}
 
 _lib = None
 

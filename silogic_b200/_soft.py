@@ -220,8 +220,117 @@ def logic_net_logits(net, x):
     return GroupSumSoft.apply(xt, B, h.num_classes, h.tau, h.feature_ste)
 
 
+# --------------------------------------------------------------- conv tree
+CONV_BUILT = {
+    "gate16": {(2, 1), (2, 2), (2, 3), (2, 4)},
+    "walsh": {(2, 1), (2, 2), (2, 3)},
+    "multilinear": {(2, 1), (2, 2), (3, 1), (3, 2), (4, 1), (4, 2), (5, 1), (6, 1)},
+    "hybrid": {(2, 1), (2, 2), (3, 1), (3, 2), (4, 1), (4, 2), (5, 1), (6, 1)},
+    "linear": {(2, 1), (2, 2), (3, 1), (4, 1), (6, 1)},
+}
+
+
+def _conv_meta(conv, wire_r=0, pool=1):
+    kind = conv.node_name
+    if kind not in CONV_BUILT or (conv.node_arity, conv.d) not in CONV_BUILT[kind]:
+        raise NotImplementedError(f"no soft conv kernel for node={kind!r} arity={conv.node_arity} "
+                                  f"depth={conv.d} in silogic_b200")
+    if conv.stride != 1:
+        raise NotImplementedError("soft conv kernels support stride 1")
+    if conv.connect == "fixed":
+        cand = conv.leaf_idx.unsqueeze(-1).to(torch.int32).contiguous()
+        conn, K, ste = None, 1, 0
+    else:
+        cand = conv.leaf_cand.to(torch.int32).contiguous()
+        conn, K, ste = conv.conn, conv.k, int(conv.gate_select == "hard")
+    if K > 16:
+        raise NotImplementedError("soft conv kernels support at most 16 candidates per leaf")
+    levels = conv.level_params()
+    if kind == "gate16":
+        params = torch.cat(list(levels), dim=1)                        # [n, nodes, 16]
+    else:
+        params = torch.cat([p.view(conv.n, -1, p.shape[-1]) for p in levels], dim=1)
+    gate_hard = 0
+    if kind == "gate16" and conv.training:
+        if conv.gate_select == "hard":
+            gate_hard = 1
+        elif conv.gate_select == "gumbel":
+            g = -torch.empty_like(params).exponential_().log()
+            params = (params + g) / conv.gumbel_tau
+            gate_hard = 1
+    inv_tau = 1.0 / conv.tau if kind == "walsh" else 1.0
+    meta = dict(cand=cand, K=K, ste=ste, node=NODE_ID[kind], arity=conv.node_arity, depth=conv.d,
+                gate_hard=gate_hard, inv_tau=float(inv_tau), kernel=conv.kh, pad=conv.padding,
+                n_out=conv.n, wire_r=wire_r, pool=pool)
+    return meta, params, conn
+
+
+class ConvSoft(torch.autograd.Function):
+    """Feature-major conv tree block (+ OR-pool): xt [C*H*W, ldb] -> [n*Hp*Wp, ldb]."""
+
+    @staticmethod
+    def forward(ctx, xt, params, conn, meta, shape):
+        require_cuda(xt)
+        xt = xt.contiguous()
+        params = params.float().contiguous()
+        connc = conn.float().contiguous() if conn is not None else None
+        C, H, W = shape
+        ldb = xt.shape[-1]
+        Ho = H + 2 * meta["pad"] - meta["kernel"] + 1
+        Wo = W + 2 * meta["pad"] - meta["kernel"] + 1
+        Hp, Wp = Ho // meta["pool"], Wo // meta["pool"]
+        y = torch.empty((meta["n_out"] * Hp * Wp, ldb), dtype=torch.float32, device=xt.device)
+        call("slg_conv_soft_fwd", ptr(xt), C, H, W, ldb, ptr(meta["cand"]), ptr(connc), meta["K"],
+             meta["ste"], meta["node"], meta["arity"], meta["depth"], ptr(params), meta["gate_hard"],
+             meta["inv_tau"], meta["kernel"], meta["pad"], meta["n_out"], meta["wire_r"],
+             meta["pool"], ptr(y), stream_ptr(xt.device))
+        ctx.save_for_backward(xt, params, connc)
+        ctx.meta, ctx.shape = meta, shape
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        xt, params, connc = ctx.saved_tensors
+        m = ctx.meta
+        C, H, W = ctx.shape
+        ldb = xt.shape[-1]
+        gy = gy.contiguous()
+        gx = torch.zeros_like(xt) if ctx.needs_input_grad[0] else None
+        gparams = torch.empty_like(params)
+        gconn = torch.empty_like(connc) if connc is not None else None
+        nbytes = lib().slg_conv_soft_workspace_bytes(H, W, ldb, m["K"], m["node"], m["arity"],
+                                                     m["depth"], m["kernel"], m["pad"], m["pool"],
+                                                     m["n_out"])
+        ws = torch.empty(max(nbytes, 4) // 4 + 1, dtype=torch.float32, device=xt.device)
+        call("slg_conv_soft_bwd", ptr(xt), C, H, W, ldb, ptr(m["cand"]), ptr(connc), m["K"], m["ste"],
+             m["node"], m["arity"], m["depth"], ptr(params), m["gate_hard"], m["inv_tau"],
+             m["kernel"], m["pad"], m["n_out"], m["wire_r"], m["pool"], ptr(gy), ptr(gx), ptr(gconn),
+             ptr(gparams), ptr(ws), ws.numel() * 4, stream_ptr(xt.device))
+        return gx, gparams, gconn, None, None
+
+
+def conv_block_fm(conv, xt, shape, wire_r=0, pool=1):
+    """One conv block on feature-major ``xt`` ([C*H*W, ldb]); returns (yt, (n, Hp, Wp))."""
+    meta, params, conn = _conv_meta(conv, wire_r, pool)
+    C, H, W = shape
+    Ho = H + 2 * conv.padding - conv.kh + 1
+    Wo = W + 2 * conv.padding - conv.kw + 1
+    return ConvSoft.apply(xt, params, conn, meta, shape), (conv.n, Ho // pool, Wo // pool)
+
+
 def logic_conv_net_features_fm(net, x):
-    raise NotImplementedError("soft conv kernels are not built yet")
+    from .layers import OrPool
+    B, C, H, W = x.shape
+    xt = ToFeatureMajor.apply(x)
+    shape = (C, H, W)
+    blocks = list(net.blocks)
+    for i in range(0, len(blocks), 2):
+        conv, pool = blocks[i], blocks[i + 1]
+        assert isinstance(pool, OrPool)
+        xt, shape = conv_block_fm(conv, xt, shape, net.wire_channels(conv, shape[0]), pool.size)
+    for layer in net.head_layers:
+        xt = fc_layer_fm(layer, xt)
+    return xt, B
 
 
 def logic_conv_net_features(net, x):
@@ -238,7 +347,11 @@ def logic_conv_net_logits(net, x):
 
 
 def conv_tree_forward(conv, x, pool=1):
-    raise NotImplementedError("soft conv kernels are not built yet")
+    """``ConvLogicTree.forward`` on ``[B, C, H, W]`` -> ``[B, n, Ho, Wo]``."""
+    require_cuda(x)
+    B, C, H, W = x.shape
+    yt, (n, Hp, Wp) = conv_block_fm(conv, ToFeatureMajor.apply(x), (C, H, W), 0, pool)
+    return FromFeatureMajor.apply(yt, B).view(B, n, Hp, Wp)
 
 
 # ------------------------------------------------------------------ OrPool

@@ -1,0 +1,97 @@
+// C-ABI entry points of the soft conv logic-tree block (kernels in conv_soft_impl.cuh).
+#include "conv_soft_impl.cuh"
+
+namespace slg {
+
+static bool conv_dispatch(int node, int arity, int depth, bool bwd, const ConvArgs& A, float* y,
+                          const float* gy, float* gx, float* ws, float* gconn, float* gparams,
+                          cudaStream_t st) {
+    switch (node) {
+        case N_GATE16: return conv_dispatch_gate16(arity, depth, bwd, A, y, gy, gx, ws, gconn, gparams, st);
+        case N_WALSH: return conv_dispatch_walsh(arity, depth, bwd, A, y, gy, gx, ws, gconn, gparams, st);
+        case N_MULTI: return conv_dispatch_multi(arity, depth, bwd, A, y, gy, gx, ws, gconn, gparams, st);
+        case N_HYBRID: return conv_dispatch_hybrid(arity, depth, bwd, A, y, gy, gx, ws, gconn, gparams, st);
+        case N_LINEAR: return conv_dispatch_linear(arity, depth, bwd, A, y, gy, gx, ws, gconn, gparams, st);
+        default: return false;
+    }
+}
+
+static int conv_check(ConvArgs& A, int64_t cin, int64_t H, int64_t W, const char* name) {
+    if (cin <= 0 || H <= 0 || W <= 0 || A.ldb <= 0 || A.n_out < 0 || A.K <= 0 || A.kernel <= 0 ||
+        A.pad < 0 || A.wire_r < 0)
+        return set_error(SLG_ERR_ARG, "%s: bad sizes", name);
+    if (A.K > CS_KMAX) return set_error(SLG_ERR_UNSUPPORTED, "%s: K=%d > %d", name, A.K, CS_KMAX);
+    if (A.pool != 1 && A.pool != 2) return set_error(SLG_ERR_UNSUPPORTED, "%s: pool must be 1 or 2", name);
+    const int64_t Ho = H + 2 * A.pad - A.kernel + 1, Wo = W + 2 * A.pad - A.kernel + 1;
+    if (Ho <= 0 || Wo <= 0) return set_error(SLG_ERR_ARG, "%s: empty output", name);
+    if (A.wire_r > 0 && (A.wire_r > cin || A.wire_r > A.n_out || Ho > H || Wo > W))
+        return set_error(SLG_ERR_ARG, "%s: wire_r needs cin >= wire_r and a same-size output", name);
+    if (!A.x || !A.cand || !A.params) return set_error(SLG_ERR_ARG, "%s: null pointer", name);
+    if (cdiv(A.ldb, 32 * CS_ITER) > 65535) return set_error(SLG_ERR_ARG, "%s: batch too large", name);
+    A.C = cin; A.H = (int)H; A.W = (int)W;
+    A.Hp = (int)(Ho / A.pool); A.Wp = (int)(Wo / A.pool);
+    if ((int64_t)A.n_out * conv_tiles(A) > 0x7fffffffLL) return set_error(SLG_ERR_ARG, "%s: grid too large", name);
+    return SLG_OK;
+}
+
+}  // namespace slg
+
+using namespace slg;
+
+extern "C" int slg_conv_soft_fwd(const float* x, int64_t cin, int64_t H, int64_t W, int64_t ldb,
+                                 const int32_t* cand, const float* conn, int32_t K, int32_t conn_ste,
+                                 int32_t node, int32_t arity, int32_t depth, const float* params,
+                                 int32_t gate_hard, float inv_tau, int32_t kernel, int32_t pad,
+                                 int64_t n_out, int64_t wire_r, int32_t pool, float* y, void* stream) {
+    ConvArgs A{x, cin, 0, 0, ldb, cand, conn, K, conn_ste, params, gate_hard, inv_tau,
+               kernel, pad, n_out, wire_r, pool, 0, 0};
+    int st = conv_check(A, cin, H, W, "slg_conv_soft_fwd");
+    if (st) return st;
+    if (!y) return set_error(SLG_ERR_ARG, "slg_conv_soft_fwd: null output");
+    if (n_out == 0 || A.Hp == 0 || A.Wp == 0) return SLG_OK;
+    if (!conv_dispatch(node, arity, depth, false, A, y, nullptr, nullptr, nullptr, nullptr, nullptr,
+                       as_stream(stream)))
+        return set_error(SLG_ERR_UNSUPPORTED, "slg_conv_soft_fwd: node %d arity %d depth %d not built",
+                         node, arity, depth);
+    return check_launch("slg_conv_soft_fwd");
+}
+
+extern "C" int64_t slg_conv_soft_workspace_bytes(int64_t H, int64_t W, int64_t ldb, int32_t K,
+                                                 int32_t node, int32_t arity, int32_t depth,
+                                                 int32_t kernel, int32_t pad, int32_t pool,
+                                                 int64_t n_out) {
+    if (arity < 2 || depth < 1 || pool < 1) return 0;
+    int64_t L = 1;
+    for (int i = 0; i < depth; ++i) L *= arity;
+    const int64_t nodes = (L - 1) / (arity - 1);
+    const int64_t npg = node == N_GATE16 ? 4 : (node == N_LINEAR ? arity + 1 : (1 << arity));
+    const int64_t Ho = H + 2 * pad - kernel + 1, Wo = W + 2 * pad - kernel + 1;
+    const int64_t npos = (Ho / pool) * (Wo / pool);
+    const int64_t tiles = cdiv(npos, CS_WARPS), chunks = cdiv(ldb, 32 * CS_ITER);
+    return tiles * chunks * n_out * (L * K + nodes * npg) * 4;
+}
+
+extern "C" int slg_conv_soft_bwd(const float* x, int64_t cin, int64_t H, int64_t W, int64_t ldb,
+                                 const int32_t* cand, const float* conn, int32_t K, int32_t conn_ste,
+                                 int32_t node, int32_t arity, int32_t depth, const float* params,
+                                 int32_t gate_hard, float inv_tau, int32_t kernel, int32_t pad,
+                                 int64_t n_out, int64_t wire_r, int32_t pool, const float* gy,
+                                 float* gx, float* gconn, float* gparams, void* workspace,
+                                 int64_t workspace_bytes, void* stream) {
+    ConvArgs A{x, cin, 0, 0, ldb, cand, conn, K, conn_ste, params, gate_hard, inv_tau,
+               kernel, pad, n_out, wire_r, pool, 0, 0};
+    int st = conv_check(A, cin, H, W, "slg_conv_soft_bwd");
+    if (st) return st;
+    if (!gy || !gparams || !workspace) return set_error(SLG_ERR_ARG, "slg_conv_soft_bwd: null pointer");
+    if (conn && !gconn) return set_error(SLG_ERR_ARG, "slg_conv_soft_bwd: gconn required with conn");
+    const int64_t need = slg_conv_soft_workspace_bytes(H, W, ldb, K, node, arity, depth, kernel, pad, pool, n_out);
+    if (workspace_bytes < need)
+        return set_error(SLG_ERR_WORKSPACE, "slg_conv_soft_bwd: workspace %lld < %lld bytes",
+                         (long long)workspace_bytes, (long long)need);
+    if (n_out == 0 || A.Hp == 0 || A.Wp == 0) return SLG_OK;
+    if (!conv_dispatch(node, arity, depth, true, A, nullptr, gy, gx, static_cast<float*>(workspace),
+                       gconn, gparams, as_stream(stream)))
+        return set_error(SLG_ERR_UNSUPPORTED, "slg_conv_soft_bwd: node %d arity %d depth %d not built",
+                         node, arity, depth);
+    return check_launch("slg_conv_soft_bwd");
+}

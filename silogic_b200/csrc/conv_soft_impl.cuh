@@ -1,0 +1,422 @@
+// Soft conv logic-tree kernels (templates): leaf gather over the k x k receptive
+// field (Top-K softmax mixture or fixed tap), an AR-ary node tree of depth D per
+// output channel, and the 2x2 OR-pool (max, first maximum in row-major window
+// order) fused into the epilogue.
+//
+// Layout: activations are [C, H, W, ldb] fp32 (batch innermost), so lane = sample
+// and every tap read is a coalesced 128-byte row segment.  A CTA = one output
+// channel (its taps / weights / node parameters staged once in shared memory) x
+// 8 pooled positions (one per warp, neighbours share L1 lines) x one batch chunk.
+//
+// Backward recomputes the window, picks the argmax position, back-propagates
+// through that position's tree, scatters dL/dx with atomics (lanes hit
+// consecutive addresses) and reduces the parameter-gradient partials over the CTA
+// into workspace rows; a per-channel finish kernel sums them deterministically and
+// applies the softmax / sigmoid Jacobians.
+#pragma once
+#include "soft_common.cuh"
+
+namespace slg {
+
+constexpr int CS_WARPS = 8;
+constexpr int CS_ITER = 8;          // samples per lane per chunk -> 256 samples / chunk
+constexpr int CS_KMAX = 16;
+
+template <int AR>
+__host__ __device__ constexpr int ipow_ar(int e) {
+    int r = 1;
+    for (int i = 0; i < e; ++i) r *= AR;
+    return r;
+}
+
+template <int AR, int D>
+struct TreeShape {
+    static constexpr int L = D == 1 ? AR : (D == 2 ? AR * AR : (D == 3 ? AR * AR * AR : AR * AR * AR * AR));
+    static constexpr int NODES = (L - 1) / (AR - 1);
+};
+
+template <int NODE, int AR>
+struct NodeStage {  // staged (transformed) parameter floats per node
+    static constexpr int NPS = NODE == N_GATE16 ? 4 : (NODE == N_LINEAR ? AR + 1 : (1 << AR) + 1);
+    static constexpr int RAW = NODE == N_GATE16 ? 16 : (NODE == N_LINEAR ? AR + 1 : (1 << AR));
+};
+
+template <int NODE, int AR, int D>
+struct ConvSmem {
+    static constexpr int L = TreeShape<AR, D>::L;
+    static constexpr int NODES = TreeShape<AR, D>::NODES;
+    int tap_c[L * CS_KMAX];
+    int tap_dy[L * CS_KMAX];
+    int tap_dx[L * CS_KMAX];
+    float w[L * CS_KMAX];
+    float np[NODES * NodeStage<NODE, AR>::NPS];
+};
+
+struct ConvArgs {
+    const float* x; int64_t C; int H; int W; int64_t ldb;
+    const int32_t* cand; const float* conn; int K; int conn_ste;
+    const float* params; int gate_hard; float inv_tau;
+    int kernel; int pad; int64_t n_out; int64_t wire_r; int pool; int Hp; int Wp;
+};
+
+// stage the channel's taps, weights and node parameters (whole block)
+template <int NODE, int AR, int D>
+__device__ __forceinline__ void conv_stage(ConvSmem<NODE, AR, D>& S, const ConvArgs& A, int64_t n) {
+    constexpr int L = TreeShape<AR, D>::L;
+    constexpr int NODES = TreeShape<AR, D>::NODES;
+    constexpr int NPS = NodeStage<NODE, AR>::NPS;
+    constexpr int RAW = NodeStage<NODE, AR>::RAW;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = A.K, kk = A.kernel * A.kernel;
+    for (int e = tid; e < L * K; e += blockDim.x) {
+        const int r = A.cand[n * L * K + e];
+        S.tap_c[e] = r / kk;
+        S.tap_dy[e] = (r % kk) / A.kernel - A.pad;
+        S.tap_dx[e] = r % A.kernel - A.pad;
+    }
+    // connection weights: warp w handles leaves w, w+8, ...
+    for (int l = warp; l < L; l += CS_WARPS) {
+        if (A.conn) {
+            if (lane == 0) {
+                const float* lg = A.conn + (n * L + l) * K;
+                float mx = lg[0];
+                int arg = 0;
+                for (int k = 1; k < K; ++k)
+                    if (lg[k] > mx) { mx = lg[k]; arg = k; }
+                float s = 0.f;
+                for (int k = 0; k < K; ++k) s += expf(lg[k] - mx);
+                for (int k = 0; k < K; ++k)
+                    S.w[l * K + k] = A.conn_ste ? (k == arg ? 1.f : 0.f) : expf(lg[k] - mx) / s;
+            }
+        } else if (lane == 0) {
+            S.w[l] = 1.0f;
+        }
+    }
+    // node parameters: warp w handles nodes w, w+8, ...
+    for (int m = warp; m < NODES; m += CS_WARPS)
+        stage_node_params<NODE, AR>(A.params + (n * NODES + m) * RAW, S.np + m * NPS, A.gate_hard,
+                                    A.inv_tau, lane);
+    __syncthreads();
+}
+
+template <int NODE, int AR, int D, int KT>
+__device__ __forceinline__ float conv_tree_value(const ConvSmem<NODE, AR, D>& S, const ConvArgs& A,
+                                                 int y, int x, int64_t b, float (&vals)[2 * TreeShape<AR, D>::L]) {
+    constexpr int L = TreeShape<AR, D>::L;
+    constexpr int NPS = NodeStage<NODE, AR>::NPS;
+    const int K = A.K;
+    // leaves into vals[0..L)
+#pragma unroll
+    for (int l = 0; l < L; ++l) {
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < KT; ++k) {
+            if (k < K) {
+                const int e = l * K + k;
+                const int iy = y + S.tap_dy[e], ix = x + S.tap_dx[e];
+                if (iy >= 0 && iy < A.H && ix >= 0 && ix < A.W)
+                    s += S.w[e] * __ldg(&A.x[(((int64_t)S.tap_c[e] * A.H + iy) * A.W + ix) * A.ldb + b]);
+            }
+        }
+        vals[l] = s;
+    }
+    // levels: level i nodes stored after the previous level's values
+    int in_base = 0, out_base = L, width = L, node_base = 0;
+#pragma unroll
+    for (int lev = 0; lev < D; ++lev) {
+        const int nn = width / AR;
+#pragma unroll
+        for (int m = 0; m < nn; ++m) {
+            float a[AR];
+#pragma unroll
+            for (int j = 0; j < AR; ++j) a[j] = vals[in_base + m * AR + j];
+            vals[out_base + m] = node_fwd<NODE, AR>(S.np + (node_base + m) * NPS, a);
+        }
+        in_base = out_base;
+        out_base += nn;
+        node_base += nn;
+        width = nn;
+    }
+    return vals[in_base];
+}
+
+template <int NODE, int AR, int D, int KT>
+__global__ void __launch_bounds__(CS_WARPS * 32)
+conv_soft_fwd_kernel(ConvArgs A, float* __restrict__ y) {
+    constexpr int L = TreeShape<AR, D>::L;
+    __shared__ ConvSmem<NODE, AR, D> S;
+    const int npos = A.Hp * A.Wp;
+    const int tiles = (npos + CS_WARPS - 1) / CS_WARPS;
+    const int64_t n = blockIdx.x / tiles;
+    const int p = (blockIdx.x % tiles) * CS_WARPS + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const bool wired = n < A.wire_r;
+    if (!wired) conv_stage<NODE, AR, D>(S, A, n);
+    if (p >= npos) return;
+    const int py = p / A.Wp, px = p % A.Wp;
+    const int64_t b0 = (int64_t)blockIdx.y * (32 * CS_ITER);
+    float vals[2 * L];
+    for (int it = 0; it < CS_ITER; ++it) {
+        const int64_t b = b0 + it * 32 + lane;
+        if (b >= A.ldb) break;
+        float best = 0.f;
+        for (int oy = 0; oy < A.pool; ++oy)
+            for (int ox = 0; ox < A.pool; ++ox) {
+                const int yy = py * A.pool + oy, xx = px * A.pool + ox;
+                const float v = wired ? __ldg(&A.x[((n * A.H + yy) * (int64_t)A.W + xx) * A.ldb + b])
+                                      : conv_tree_value<NODE, AR, D, KT>(S, A, yy, xx, b, vals);
+                if ((oy | ox) == 0 || v > best) best = v;
+            }
+        y[((n * npos) + p) * A.ldb + b] = best;
+    }
+}
+
+// workspace rows: ws[(blockIdx.y * tiles + tile) * n_out + n][NPART],
+// NPART = L*K (conn) + NODES*NPG (node)
+template <int NODE, int AR, int D, int KT>
+__global__ void __launch_bounds__(CS_WARPS * 32)
+conv_soft_bwd_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict__ gx,
+                     float* __restrict__ ws, int npart) {
+    constexpr int L = TreeShape<AR, D>::L;
+    constexpr int NODES = TreeShape<AR, D>::NODES;
+    constexpr int NPS = NodeStage<NODE, AR>::NPS;
+    constexpr int NPG = NodeSize<NODE, AR>::NPG;
+    __shared__ ConvSmem<NODE, AR, D> S;
+    __shared__ float red[CS_WARPS][L * KT + NODES * NPG];
+    const int npos = A.Hp * A.Wp;
+    const int tiles = (npos + CS_WARPS - 1) / CS_WARPS;
+    const int64_t n = blockIdx.x / tiles;
+    const int tile = blockIdx.x % tiles;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int p = tile * CS_WARPS + warp;
+    const bool wired = n < A.wire_r;
+    float* wrow = ws + (((int64_t)blockIdx.y * tiles + tile) * A.n_out + n) * npart;
+    if (wired) {
+        for (int e = threadIdx.x; e < npart; e += blockDim.x) wrow[e] = 0.f;
+        if (p >= npos || !gx) return;
+        const int py = p / A.Wp, px = p % A.Wp;
+        const int64_t b0 = (int64_t)blockIdx.y * (32 * CS_ITER);
+        for (int it = 0; it < CS_ITER; ++it) {
+            const int64_t b = b0 + it * 32 + lane;
+            if (b >= A.ldb) break;
+            float best = 0.f;
+            int64_t bi = 0;
+            for (int oy = 0; oy < A.pool; ++oy)
+                for (int ox = 0; ox < A.pool; ++ox) {
+                    const int64_t idx = ((n * A.H + py * A.pool + oy) * (int64_t)A.W + px * A.pool + ox) * A.ldb + b;
+                    const float v = __ldg(&A.x[idx]);
+                    if ((oy | ox) == 0 || v > best) { best = v; bi = idx; }
+                }
+            atomicAdd(&gx[bi], gy[((n * npos) + p) * A.ldb + b]);
+        }
+        return;
+    }
+    conv_stage<NODE, AR, D>(S, A, n);
+    float acc_w[L * KT];
+#pragma unroll
+    for (int e = 0; e < L * KT; ++e) acc_w[e] = 0.f;
+    float acc_n[NODES][NPG];
+#pragma unroll
+    for (int m = 0; m < NODES; ++m)
+#pragma unroll
+        for (int q = 0; q < NPG; ++q) acc_n[m][q] = 0.f;
+
+    if (p < npos) {
+        const int py = p / A.Wp, px = p % A.Wp;
+        const int64_t b0 = (int64_t)blockIdx.y * (32 * CS_ITER);
+        float vals[2 * L];
+        for (int it = 0; it < CS_ITER; ++it) {
+            const int64_t b = b0 + it * 32 + lane;
+            if (b >= A.ldb) break;
+            const float g = gy[((n * npos) + p) * A.ldb + b];
+            // argmax position of the pool window (first maximum)
+            int by = py * A.pool, bx = px * A.pool;
+            if (A.pool > 1) {
+                float best = 0.f;
+                for (int oy = 0; oy < A.pool; ++oy)
+                    for (int ox = 0; ox < A.pool; ++ox) {
+                        const int yy = py * A.pool + oy, xx = px * A.pool + ox;
+                        const float v = conv_tree_value<NODE, AR, D, KT>(S, A, yy, xx, b, vals);
+                        if ((oy | ox) == 0 || v > best) { best = v; by = yy; bx = xx; }
+                    }
+            }
+            conv_tree_value<NODE, AR, D, KT>(S, A, by, bx, b, vals);
+            // reverse pass through the tree: adjoints indexed like vals; level bases:
+            // leaves at 0, level i (1..D) at L + sum_{j<i} L/AR^j
+            float adj[2 * L];
+            int base[D + 1];
+            base[0] = 0;
+            {
+                int b_ = L, wdt = L;
+#pragma unroll
+                for (int lev = 1; lev <= D; ++lev) { base[lev] = b_; wdt /= AR; b_ += wdt; }
+            }
+            adj[base[D]] = g;
+            int node_base = NODES;   // nodes of level lev occupy [node_base - count, node_base)
+#pragma unroll
+            for (int lev = D; lev >= 1; --lev) {
+                const int cnt = L / ipow_ar<AR>(lev);
+                node_base -= cnt;
+#pragma unroll
+                for (int m = 0; m < cnt; ++m) {
+                    float a[AR], ga[AR];
+#pragma unroll
+                    for (int j = 0; j < AR; ++j) a[j] = vals[base[lev - 1] + m * AR + j];
+                    node_bwd<NODE, AR>(S.np + (node_base + m) * NPS, a, adj[base[lev] + m], ga,
+                                       acc_n[node_base + m]);
+#pragma unroll
+                    for (int j = 0; j < AR; ++j) adj[base[lev - 1] + m * AR + j] = ga[j];
+                }
+            }
+            // leaves -> taps
+            const int K = A.K;
+#pragma unroll
+            for (int l = 0; l < L; ++l) {
+                const float gl = adj[l];
+#pragma unroll
+                for (int k = 0; k < KT; ++k) {
+                    if (k < K) {
+                        const int e = l * K + k;
+                        const int iy = by + S.tap_dy[e], ix = bx + S.tap_dx[e];
+                        if (iy >= 0 && iy < A.H && ix >= 0 && ix < A.W) {
+                            const int64_t idx = (((int64_t)S.tap_c[e] * A.H + iy) * A.W + ix) * A.ldb + b;
+                            acc_w[l * KT + k] += gl * __ldg(&A.x[idx]);
+                            if (gx) atomicAdd(&gx[idx], gl * S.w[e]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    // reduce partials: warp, then across the CTA's warps
+#pragma unroll
+    for (int e = 0; e < L * KT; ++e) {
+        const float s = warp_sum(acc_w[e]);
+        if (lane == 0) red[warp][e] = s;
+    }
+#pragma unroll
+    for (int m = 0; m < NODES; ++m)
+#pragma unroll
+        for (int q = 0; q < NPG; ++q) {
+            const float s = warp_sum(acc_n[m][q]);
+            if (lane == 0) red[warp][L * KT + m * NPG + q] = s;
+        }
+    __syncthreads();
+    const int K = A.K;
+    for (int e = threadIdx.x; e < L * K + NODES * NPG; e += blockDim.x) {
+        const int src = e < L * K ? (e / K) * KT + (e % K) : L * KT + (e - L * K);
+        float s = 0.f;
+        for (int w = 0; w < CS_WARPS; ++w) s += red[w][src];
+        wrow[e] = s;
+    }
+}
+
+// one thread per output channel: sum the workspace rows and apply the Jacobians
+template <int NODE, int AR, int D>
+__global__ void conv_soft_finish_kernel(const float* __restrict__ ws, int64_t rows, ConvArgs A,
+                                        int npart, float* __restrict__ gconn, float* __restrict__ gparams) {
+    constexpr int L = TreeShape<AR, D>::L;
+    constexpr int NODES = TreeShape<AR, D>::NODES;
+    constexpr int NPG = NodeSize<NODE, AR>::NPG;
+    constexpr int RAW = NodeStage<NODE, AR>::RAW;
+    const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= A.n_out) return;
+    const int K = A.K;
+    const bool dead = n < A.wire_r;
+    float tot[L * CS_KMAX + NODES * NPG];
+    for (int e = 0; e < npart; ++e) tot[e] = 0.f;
+    for (int64_t r = 0; r < rows; ++r) {
+        const float* row = ws + (r * A.n_out + n) * npart;
+        for (int e = 0; e < npart; ++e) tot[e] += row[e];
+    }
+    if (gconn) {
+        for (int l = 0; l < L; ++l) {
+            const float* lg = A.conn + (n * L + l) * K;
+            float mx = lg[0];
+            for (int k = 1; k < K; ++k) mx = fmaxf(mx, lg[k]);
+            float s = 0.f;
+            for (int k = 0; k < K; ++k) s += expf(lg[k] - mx);
+            float dot = 0.f;
+            for (int k = 0; k < K; ++k) dot += expf(lg[k] - mx) / s * tot[l * K + k];
+            for (int k = 0; k < K; ++k)
+                gconn[(n * L + l) * K + k] = dead ? 0.f : expf(lg[k] - mx) / s * (tot[l * K + k] - dot);
+        }
+    }
+    for (int m = 0; m < NODES; ++m) {
+        const float* g = tot + L * K + m * NPG;
+        const float* raw = A.params + (n * NODES + m) * RAW;
+        float* out = gparams + (n * NODES + m) * RAW;
+        if constexpr (NODE == N_GATE16) {
+            float mx = raw[0];
+            for (int i = 1; i < 16; ++i) mx = fmaxf(mx, raw[i]);
+            float e[16], s = 0.f;
+            for (int i = 0; i < 16; ++i) { e[i] = expf(raw[i] - mx); s += e[i]; }
+            float gp[16], dot = 0.f;
+            for (int i = 0; i < 16; ++i) {
+                gp[i] = c_basis[i][0] * g[0] + c_basis[i][1] * g[1] + c_basis[i][2] * g[2] + c_basis[i][3] * g[3];
+                dot += (e[i] / s) * gp[i];
+            }
+            for (int i = 0; i < 16; ++i) out[i] = dead ? 0.f : (e[i] / s) * (gp[i] - dot);
+        } else if constexpr (NODE == N_MULTI || NODE == N_HYBRID) {
+            for (int q = 0; q < (1 << AR); ++q) {
+                const float sg = sigmoidf_(raw[q]);
+                out[q] = dead ? 0.f : g[q] * sg * (1.f - sg);
+            }
+        } else {
+            for (int q = 0; q < NPG; ++q) out[q] = dead ? 0.f : g[q];
+        }
+    }
+}
+
+// ------------------------------------------------------------ launchers
+inline int conv_tiles(const ConvArgs& A) { return (A.Hp * A.Wp + CS_WARPS - 1) / CS_WARPS; }
+inline int64_t conv_chunks(const ConvArgs& A) { return cdiv(A.ldb, 32 * CS_ITER); }
+
+template <int NODE, int AR, int D, int KT>
+inline void conv_launch_fwd(const ConvArgs& A, float* y, cudaStream_t st) {
+    dim3 grid((unsigned)(A.n_out * conv_tiles(A)), (unsigned)conv_chunks(A));
+    conv_soft_fwd_kernel<NODE, AR, D, KT><<<grid, CS_WARPS * 32, 0, st>>>(A, y);
+}
+
+template <int NODE, int AR, int D, int KT>
+inline void conv_launch_bwd(const ConvArgs& A, const float* gy, float* gx, float* ws, float* gconn,
+                            float* gparams, cudaStream_t st) {
+    constexpr int L = TreeShape<AR, D>::L;
+    constexpr int NODES = TreeShape<AR, D>::NODES;
+    const int npart = L * A.K + NODES * NodeSize<NODE, AR>::NPG;
+    dim3 grid((unsigned)(A.n_out * conv_tiles(A)), (unsigned)conv_chunks(A));
+    conv_soft_bwd_kernel<NODE, AR, D, KT><<<grid, CS_WARPS * 32, 0, st>>>(A, gy, gx, ws, npart);
+    const int64_t rows = conv_chunks(A) * conv_tiles(A);
+    conv_soft_finish_kernel<NODE, AR, D><<<(unsigned)cdiv(A.n_out, 64), 64, 0, st>>>(ws, rows, A, npart,
+                                                                                      gconn, gparams);
+}
+
+template <int NODE, int AR, int D>
+inline void conv_launch_k(bool bwd, const ConvArgs& A, float* y, const float* gy, float* gx, float* ws,
+                          float* gconn, float* gparams, cudaStream_t st) {
+    if (A.K == 1) {
+        if (bwd) conv_launch_bwd<NODE, AR, D, 1>(A, gy, gx, ws, gconn, gparams, st);
+        else conv_launch_fwd<NODE, AR, D, 1>(A, y, st);
+    } else if (A.K <= 4) {
+        if (bwd) conv_launch_bwd<NODE, AR, D, 4>(A, gy, gx, ws, gconn, gparams, st);
+        else conv_launch_fwd<NODE, AR, D, 4>(A, y, st);
+    } else if (A.K <= 8) {
+        if (bwd) conv_launch_bwd<NODE, AR, D, 8>(A, gy, gx, ws, gconn, gparams, st);
+        else conv_launch_fwd<NODE, AR, D, 8>(A, y, st);
+    } else {
+        if (bwd) conv_launch_bwd<NODE, AR, D, 16>(A, gy, gx, ws, gconn, gparams, st);
+        else conv_launch_fwd<NODE, AR, D, 16>(A, y, st);
+    }
+}
+
+#define SLG_CONV_DISPATCH_DECL(NAME)                                                              \
+    bool conv_dispatch_##NAME(int arity, int depth, bool bwd, const ConvArgs& A, float* y,        \
+                              const float* gy, float* gx, float* ws, float* gconn, float* gparams, \
+                              cudaStream_t st);
+SLG_CONV_DISPATCH_DECL(gate16)
+SLG_CONV_DISPATCH_DECL(walsh)
+SLG_CONV_DISPATCH_DECL(multi)
+SLG_CONV_DISPATCH_DECL(hybrid)
+SLG_CONV_DISPATCH_DECL(linear)
+
+}  // namespace slg

@@ -32,6 +32,32 @@ def assert_logits_close(logits, ref, feat_ref, tau):
     assert np.all(d <= near + 1e-3), f"logit counts differ beyond threshold ties: {d.max()}"
 
 
+def _conv_grads_vs_oracle(name, m, enc, z, x):
+    import json
+    from oracle import soft as OS
+    from oracle.spec import net_spec
+    with torch.no_grad():
+        xs = encoder_image(enc(x), z) if enc is not None else x
+    routing = our_pool_routing(m, xs.detach())
+    sd = {k: v.detach().cpu() for k, v in m.state_dict().items()}
+    spec = net_spec(str(z["ctor"]), json.loads(str(z["kwargs"])), {k: v.numpy() for k, v in sd.items()})
+    P = OS.params_from_sd(sd)
+    xr = torch.from_numpy(z["x"]).clone().requires_grad_(True)
+    xo = xr
+    thr = None
+    if enc is not None:
+        thr = torch.from_numpy(z["encsd/thresholds"]).clone().requires_grad_(True)
+        xo = encoder_image(OS.learned_thermometer(xr, thr), z)
+    feat = OS.net_features(spec, P, xo, training=True, pool_index=routing)
+    lo = OS.group_sum(feat, spec["num_classes"], spec["tau"])
+    (lo * torch.from_numpy(z["rmat"])).sum().backward()
+    assert_grad_close(x.grad, xr.grad.numpy(), f"{name} x")
+    for n, p in m.named_parameters():
+        assert_grad_close(p.grad, P[n].grad.numpy(), f"{name} {n}")
+    if enc is not None:
+        assert_grad_close(enc.thresholds.grad, thr.grad.numpy(), "encoder thresholds")
+
+
 def run_soft(name):
     m, enc, z, _ = build_model(name, dev)
     m.train()
@@ -45,18 +71,27 @@ def run_soft(name):
     return m, enc, z, x, feat, logits
 
 
-@pytest.mark.parametrize("name", FC)
-def test_fc_soft_matches_reference_golden(name):
+@pytest.mark.parametrize("name", FIXTURES)
+def test_soft_matches_reference_golden(name):
+    """Forward: strict vs the reference.  Gradients: FC nets strict vs the reference;
+    conv nets (OR-pool) strict vs the oracle -- itself pinned to these fixtures on the
+    CPU -- replaying this package's pool routing, because the reference's choice at
+    windows tied within fp32 rounding depends on its own rounding."""
     m, enc, z, x, feat, logits = run_soft(name)
     np.testing.assert_allclose(feat.detach().cpu().numpy(), z["feat"], rtol=1e-5, atol=1e-6)
     assert_logits_close(logits.detach().cpu().numpy(), z["logits"], z["feat"], m.head.tau)
     params = dict(m.named_parameters())
+    if name.startswith("conv_"):
+        _conv_grads_vs_oracle(name, m, enc, z, x)
+        return
     for k in z.files:
         if k.startswith("grad/"):
             n = k[5:]
             got = x.grad if n == "x" else params[n].grad
             assert got is not None, n
             assert_grad_close(got, z[k], f"{name} grad {n}")
+    if enc is not None:
+        assert_grad_close(enc.thresholds.grad, z["encgrad/thresholds"], "encoder thresholds")
 
 
 def _rand_model(ctor, kw, seed):
@@ -70,14 +105,37 @@ def _rand_model(ctor, kw, seed):
     return m
 
 
-def oracle_soft(ctor, kw, m, x, rmat):
+@torch.no_grad()
+def our_pool_routing(m, x):
+    """Per conv block, the window element our first-max OR-pool selects (flat index into
+    H*W), computed from this package's own unpooled block outputs."""
+    idx, h = [], x
+    blocks = list(m.blocks)
+    for i in range(0, len(blocks), 2):
+        conv = blocks[i]
+        y = conv(h)                                              # unpooled, our kernel
+        r = m.wire_channels(conv, h.shape[1])
+        if r:
+            y = torch.cat([h[:, :r], y[:, r:]], 1)
+        B, n, H, W = y.shape
+        Hp, Wp = H // 2, W // 2
+        win = y[:, :, :Hp * 2, :Wp * 2].reshape(B, n, Hp, 2, Wp, 2).permute(0, 1, 2, 4, 3, 5)
+        a = win.reshape(B, n, Hp, Wp, 4).argmax(-1)              # first maximum
+        hp = torch.arange(Hp, device=y.device).view(1, 1, Hp, 1)
+        wp = torch.arange(Wp, device=y.device).view(1, 1, 1, Wp)
+        idx.append(((2 * hp + a // 2) * W + 2 * wp + a % 2).cpu())
+        h = torch.nn.functional.max_pool2d(y, 2, 2)
+    return idx
+
+
+def oracle_soft(ctor, kw, m, x, rmat, pool_index=None):
     from oracle import soft as OS
     from oracle.spec import net_spec
     sd = {k: v.detach().cpu() for k, v in m.state_dict().items()}
     spec = net_spec(ctor, kw, {k: v.numpy() for k, v in sd.items()})
     P = OS.params_from_sd(sd)
     xr = x.detach().cpu().clone().requires_grad_(True)
-    feat = OS.net_features(spec, P, xr, training=True)
+    feat = OS.net_features(spec, P, xr, training=True, pool_index=pool_index)
     logits = OS.group_sum(feat, spec["num_classes"], spec["tau"])
     (logits * rmat).sum().backward()
     return feat.detach().numpy(), logits.detach().numpy(), P, xr.grad
@@ -169,3 +227,55 @@ def test_groupsum_orpool_thermometer_soft():
     ref.backward(gg.cpu())
     assert_grad_close(xe.grad, xc.grad.numpy(), "enc x")
     assert_grad_close(enc.thresholds.grad, thr.grad.numpy(), "enc thr")
+
+
+@pytest.mark.parametrize("kw", [
+    dict(in_channels=15, in_hw=16, channels=[32, 64], head_widths=[320], tree_depth=2,
+         node="gate16", tau=20.0, seed=0),
+    dict(in_channels=6, in_hw=12, channels=[16, 24], head_widths=[90], tree_depth=3,
+         node="gate16", connect="fixed", tau=3.0, seed=1, wire_residual=0.5),
+    dict(in_channels=9, in_hw=12, channels=[16, 24], head_widths=[120, 60], tree_depth=1,
+         node="multilinear", arity=6, k=8, n_chan=4, gate_select="hard", tau=12.0, seed=2),
+    dict(in_channels=6, in_hw=10, channels=[12, 20], head_widths=[100], tree_depth=2,
+         node="walsh", k=16, n_chan=2, tau=5.0, seed=3),
+    dict(in_channels=6, in_hw=10, channels=[12, 20], head_widths=[100], tree_depth=2,
+         node="hybrid", arity=3, k=4, tau=5.0, seed=4),
+], ids=["gate16_topk_d2", "gate16_fixed_d3_wire", "multilinear6_ste", "walsh_k16_d2", "hybrid3_d2"])
+@pytest.mark.parametrize("B", [3, 300])
+def test_conv_soft_vs_oracle(kw, B):
+    m = _rand_model("LogicConvNet", kw, 21)
+    g = torch.Generator().manual_seed(B)
+    C, hw = kw["in_channels"], kw["in_hw"]
+    x = (torch.rand(B, C, hw, hw, generator=g) < 0.5).float()
+    rmat = torch.randn(B, 10, generator=g)
+    routing = our_pool_routing(m.to(dev).train(), x.to(dev))
+    f_ref, l_ref, P, gx_ref = oracle_soft("LogicConvNet", kw, m.cpu(), x, rmat, routing)
+    m = m.to(dev).train()
+    xd = x.to(dev).requires_grad_(True)
+    feat = m._run(xd, hard=False)
+    np.testing.assert_allclose(feat.detach().cpu().numpy(), f_ref, rtol=1e-5, atol=1e-6)
+    logits = m(xd)
+    assert_logits_close(logits.detach().cpu().numpy(), l_ref, f_ref, m.head.tau)
+    (logits * rmat.to(dev)).sum().backward()
+    assert_grad_close(xd.grad, gx_ref.numpy(), "x")
+    for n, p in m.named_parameters():
+        assert_grad_close(p.grad, P[n].grad.numpy(), n)
+
+
+def test_conv_layer_soft_unpooled_vs_oracle():
+    import silogic_b200 as S
+    from oracle import soft as OS
+    from oracle.spec import conv_block_spec
+    torch.manual_seed(1)
+    conv = S.ConvLogicTree(5, 12, tree_depth=2, connect="topk", k=4, seed=7)
+    with torch.no_grad():
+        for p in conv.parameters():
+            p.normal_()
+    x = torch.rand(40, 5, 9, 7)
+    sd = {k: v.detach() for k, v in conv.state_dict().items()}
+    Bk = conv_block_spec({k: v.numpy() for k, v in sd.items()}, "", 5, 12, 3, 2, "topk", 4,
+                         "gate16", 2, "softmax", 1.0)
+    P = OS.params_from_sd(sd)
+    ref = OS.conv_block(Bk, P, x, training=True)
+    got = conv.to(dev)(x.to(dev))
+    np.testing.assert_allclose(got.detach().cpu().numpy(), ref.detach().numpy(), rtol=1e-5, atol=1e-6)
