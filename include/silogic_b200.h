@@ -146,6 +146,22 @@ int slg_fc_soft_bwd(const float* x, int64_t in_dim, int64_t ldb, const int32_t* 
                     int64_t wire_r, const float* gy, float* gx, float* gconn, float* gparams,
                     void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Allocation-free form of slg_fc_soft_bwd, for callers that cannot allocate
+ * device memory (a plugin inside a host framework that owns all device buffers,
+ * or a latency-critical loop that must never enter the allocator).  It has no
+ * counterpart in the reference.  Its scratch is a static device array of
+ * SLG_FC_NOALLOC_SCRATCH_BYTES per GPU, resident until process exit; sizes whose
+ * slg_fc_soft_workspace_bytes exceed it fail with SLG_ERR_WORKSPACE.  The first
+ * call on a device looks up the array's address (make it before any stream
+ * capture).  All calls on a device share the array: calls that overlap on the
+ * GPU race.  Same arguments and results as slg_fc_soft_bwd otherwise. */
+#define SLG_FC_NOALLOC_SCRATCH_BYTES (16ll << 20)
+int slg_fc_soft_bwd_noalloc(const float* x, int64_t in_dim, int64_t ldb, const int32_t* cand,
+                            const float* conn, int32_t K, int32_t conn_ste, int32_t node,
+                            int32_t arity, const float* params, int32_t gate_hard, float inv_tau,
+                            int64_t out_dim, int64_t wire_r, const float* gy, float* gx,
+                            float* gconn, float* gparams, void* stream);
+
 /* -------------------------------------------------- soft-path boundaries */
 
 /* [B, F] sample-major -> [F, ldb] feature-major (columns >= B zeroed), and back. */
