@@ -162,6 +162,43 @@ int slg_fc_soft_bwd_noalloc(const float* x, int64_t in_dim, int64_t ldb, const i
                             int64_t out_dim, int64_t wire_r, const float* gy, float* gx,
                             float* gconn, float* gparams, void* stream);
 
+/* ------------------------------------------------------ soft conv block */
+
+/* Soft forward of one conv logic-tree block on feature-major x [cin, H, W, ldb]:
+ * leaf l of output channel n at position (y, x) = sum_k w[n,l,k] x[c, y+dy-pad, x+dx-pad]
+ * over candidate taps cand[n,l,k] = c*k*k + dy*k + dx (w = softmax(conn), one-hot when
+ * conn_ste, or conn == NULL with K = 1 for fixed leaves); an arity-ary tree of `depth`
+ * levels of `node` nodes (params [n, total_nodes, P] raw, level 0 first) combines the
+ * leaves; channels n < wire_r copy input channel n; pool 2 takes the 2x2 max
+ * (OR-pool) in the epilogue.  y is [n_out, Ho/pool, Wo/pool, ldb].
+ * Replaces tree_conv / tree_conv_topk / conv_hybrid (silogic/kernels/conv.py:354-400,
+ * conv_topk.py:139-189, conv_hybrid.py:161-213), the PyTorch path of
+ * ConvLogicTree.forward (silogic/layers.py:448-485) and OrPool.forward
+ * (silogic/layers.py:558-559) fused behind it. */
+int slg_conv_soft_fwd(const float* x, int64_t cin, int64_t H, int64_t W, int64_t ldb,
+                      const int32_t* cand, const float* conn, int32_t K, int32_t conn_ste,
+                      int32_t node, int32_t arity, int32_t depth, const float* params,
+                      int32_t gate_hard, float inv_tau, int32_t kernel, int32_t pad,
+                      int64_t n_out, int64_t wire_r, int32_t pool, float* y, void* stream);
+
+/* Bytes of scratch slg_conv_soft_bwd needs (per-CTA parameter-gradient partials). */
+int64_t slg_conv_soft_workspace_bytes(int64_t H, int64_t W, int64_t ldb, int32_t K, int32_t node,
+                                      int32_t arity, int32_t depth, int32_t kernel, int32_t pad,
+                                      int32_t pool, int64_t n_out);
+
+/* Backward of slg_conv_soft_fwd given gy [n_out, Ho/pool, Wo/pool, ldb]: routes each
+ * pooled gradient to the first maximum of its window, back-propagates through the
+ * tree, accumulates gx (caller zero-fills; NULL = skip) and writes gconn / gparams.
+ * Replaces TreeConvFn / TreeConvTopkFn / ConvHybridFn.backward (conv.py:379-396,
+ * conv_topk.py:156-172, conv_hybrid.py:179-193). */
+int slg_conv_soft_bwd(const float* x, int64_t cin, int64_t H, int64_t W, int64_t ldb,
+                      const int32_t* cand, const float* conn, int32_t K, int32_t conn_ste,
+                      int32_t node, int32_t arity, int32_t depth, const float* params,
+                      int32_t gate_hard, float inv_tau, int32_t kernel, int32_t pad,
+                      int64_t n_out, int64_t wire_r, int32_t pool, const float* gy, float* gx,
+                      float* gconn, float* gparams, void* workspace, int64_t workspace_bytes,
+                      void* stream);
+
 /* -------------------------------------------------- soft-path boundaries */
 
 /* [B, F] sample-major -> [F, ldb] feature-major (columns >= B zeroed), and back. */
