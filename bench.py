@@ -186,6 +186,7 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
     torch.cuda.synchronize()
     times = []
     with ClockSampler(torch.cuda.current_device()) as clk:
+        torch.cuda.nvtx.range_push("timed_hard")
         for _ in range(steps):
             flush.fill_(1)
             e0 = torch.cuda.Event(enable_timing=True)
@@ -195,6 +196,7 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
             e1.record()
             times.append((e0, e1))
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
         ms = statistics.mean(a.elapsed_time(b) for a, b in times)
         e2e_times = []
         for _ in range(steps):
@@ -256,6 +258,7 @@ def run_soft(cfg, B, steps, warmup, rank, ws, dev):
     if ws > 1:
         torch.distributed.barrier()
     times = []
+    torch.cuda.nvtx.range_push("timed_soft")
     for _ in range(steps):
         flush.fill_(1)
         e0 = torch.cuda.Event(enable_timing=True)
@@ -265,6 +268,7 @@ def run_soft(cfg, B, steps, warmup, rank, ws, dev):
         e1.record()
         times.append((e0, e1))
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     ms = statistics.mean(a.elapsed_time(b) for a, b in times)
     return dict(ms=ms)
 

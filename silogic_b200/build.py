@@ -34,9 +34,23 @@ def _nvcc():
     raise RuntimeError("nvcc not found")
 
 
-def _deps_digest():
+def _includes(path, seen):
+    """Local headers a source includes, transitively."""
+    import re
+    with open(path) as f:
+        for name in re.findall(r'#include\s+"([^"]+)"', f.read()):
+            for d in (os.path.dirname(path), CSRC, INCLUDE):
+                q = os.path.join(d, name)
+                if os.path.exists(q) and q not in seen:
+                    seen.add(q)
+                    _includes(q, seen)
+                    break
+    return seen
+
+
+def _deps_digest(src):
     h = hashlib.sha1(" ".join(ARCH + FLAGS).encode())
-    for p in sorted(glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h"))):
+    for p in sorted(_includes(src, set())):
         with open(p, "rb") as f:
             h.update(f.read())
     return h.hexdigest()
@@ -62,10 +76,9 @@ def build(force=False, jobs=8, verbose=False, extra=()):
     """Compile and link; returns the path of the shared library."""
     os.makedirs(BUILD, exist_ok=True)
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
-    digest = _deps_digest()
     extra = list(extra)
     with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
-        res = list(ex.map(lambda s: _compile(s, force, digest, extra), srcs))
+        res = list(ex.map(lambda s: _compile(s, force, _deps_digest(s), extra), srcs))
     errs = [e for _, e in res if e]
     if errs:
         raise RuntimeError("nvcc failed:\n" + "\n".join(errs))

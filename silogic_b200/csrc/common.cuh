@@ -1,6 +1,7 @@
 // Shared helpers for the silogic_b200 CUDA kernels (sm_100a only).
 #pragma once
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <stdint.h>
 
 #include "silogic_b200.h"

@@ -63,6 +63,17 @@ fc_soft_fwd_kernel(const float4* __restrict__ x, int64_t nv, const int32_t* __re
     }
     FcSmem<NODE, AR>& S = smem[warp];
     stage_node<NODE, AR>(S, o, cand, conn, K, conn_ste, params, np_stride, gate_hard, inv_tau, lane);
+    // warp-uniform wiring and weights live in registers for the whole chunk
+    const float4* rows[AR * KT];
+    float wr[AR * KT];
+#pragma unroll
+    for (int j = 0; j < AR; ++j)
+#pragma unroll
+        for (int k = 0; k < KT; ++k) {
+            const bool on = k < K;
+            rows[j * KT + k] = x + (on ? (int64_t)S.cand[j * K + k] * nv : 0);
+            wr[j * KT + k] = on ? S.w[j * K + k] : 0.0f;
+        }
     for (int it = 0; it < FS_ITER; ++it) {
         const int64_t v = v0 + it * 32 + lane;
         if (v >= nv) break;
@@ -73,8 +84,8 @@ fc_soft_fwd_kernel(const float4* __restrict__ x, int64_t nv, const int32_t* __re
 #pragma unroll
             for (int k = 0; k < KT; ++k) {
                 if (k < K) {
-                    const float wk = S.w[j * K + k];
-                    const float4 xv = __ldg(&x[(int64_t)S.cand[j * K + k] * nv + v]);
+                    const float wk = wr[j * KT + k];
+                    const float4 xv = __ldg(rows[j * KT + k] + v);
                     acc.x += wk * xv.x; acc.y += wk * xv.y; acc.z += wk * xv.z; acc.w += wk * xv.w;
                 }
             }

@@ -135,34 +135,53 @@ conv_hard_kernel(const uint4* __restrict__ x, int64_t cin, int H, int W, int64_t
 }
 
 // --------------------------------------------------------------- GroupSum
-// One thread: class c, one 32-bit word (32 samples).  Bit-sliced vertical
-// counters: plane l holds bit l of every sample's running count, so adding a
-// row costs a short carry ripple instead of 32 per-sample adds.
-__global__ void __launch_bounds__(HB_THREADS)
+// CTA = one class x 32 consecutive 32-bit words (1024 samples); its 8 warps split
+// the class's G rows into 8 segments.  Each thread keeps bit-sliced vertical
+// counters for its word (plane l = bit l of every sample's running count), so
+// adding a row is a short carry ripple over LEVELS planes instead of 32
+// per-sample adds; the 8 segment counts are then summed through shared memory.
+constexpr int GS_SEG = 8;
+
+template <int LEVELS>
+__global__ void __launch_bounds__(256)
 groupsum_kernel(const uint32_t* __restrict__ x, int64_t G, int64_t ld32, int64_t B, int C,
                 int32_t* __restrict__ counts) {
-    const int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    __shared__ int32_t cnt[GS_SEG][1024 + 8];
+    const int lane = threadIdx.x & 31, seg = threadIdx.x >> 5;
     const int c = blockIdx.y;
-    if (w * 32 >= B) return;
-    uint32_t plane[20];
+    const int64_t w = (int64_t)blockIdx.x * 32 + lane;
+    const int64_t per = (G + GS_SEG - 1) / GS_SEG;
+    const int64_t g0 = seg * per, g1 = min(G, g0 + per);
+    uint32_t plane[LEVELS];
 #pragma unroll
-    for (int l = 0; l < 20; ++l) plane[l] = 0;
-    const uint32_t* base = x + (int64_t)c * G * ld32 + w;
-    for (int64_t g = 0; g < G; ++g) {
-        uint32_t carry = __ldg(base + g * ld32);
+    for (int l = 0; l < LEVELS; ++l) plane[l] = 0;
+    if (w * 32 < B) {
+        const uint32_t* base = x + (int64_t)c * G * ld32 + w;
+        for (int64_t g = g0; g < g1; ++g) {
+            uint32_t carry = __ldg(base + g * ld32);
 #pragma unroll
-        for (int l = 0; l < 20; ++l) {
-            const uint32_t t = plane[l] & carry;
-            plane[l] ^= carry;
-            carry = t;
+            for (int l = 0; l < LEVELS; ++l) {
+                const uint32_t t = plane[l] & carry;
+                plane[l] ^= carry;
+                carry = t;
+            }
         }
     }
-    const int64_t s_end = min((int64_t)32, B - w * 32);
-    for (int s = 0; s < s_end; ++s) {
-        int32_t cnt = 0;
+#pragma unroll 4
+    for (int s = 0; s < 32; ++s) {
+        int32_t v = 0;
 #pragma unroll
-        for (int l = 0; l < 20; ++l) cnt |= (int32_t)((plane[l] >> s) & 1u) << l;
-        counts[(w * 32 + s) * C + c] = cnt;
+        for (int l = 0; l < LEVELS; ++l) v |= (int32_t)((plane[l] >> s) & 1u) << l;
+        cnt[seg][lane * 32 + s] = v;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 1024; i += 256) {
+        const int64_t b = (int64_t)blockIdx.x * 1024 + i;
+        if (b >= B) continue;
+        int32_t v = 0;
+#pragma unroll
+        for (int q = 0; q < GS_SEG; ++q) v += cnt[q][i];
+        counts[b * C + c] = v;
     }
 }
 
@@ -260,12 +279,17 @@ extern "C" int slg_groupsum(const uint64_t* x, int64_t width, int64_t ldw, int64
     if (width % num_classes) return set_error(SLG_ERR_ARG, "slg_groupsum: width %% num_classes != 0");
     if (ldw < cdiv(B, 64)) return set_error(SLG_ERR_ARG, "slg_groupsum: ldw too small");
     const int64_t G = width / num_classes;
-    if (G >= (1 << 20)) return set_error(SLG_ERR_UNSUPPORTED, "slg_groupsum: group too large");
+    if (G >= (1ll << 20)) return set_error(SLG_ERR_UNSUPPORTED, "slg_groupsum: group too large");
+    if (cdiv(B, 1024) > 0x7fffffffLL || num_classes > 65535)
+        return set_error(SLG_ERR_ARG, "slg_groupsum: grid too large");
     if (B == 0) return SLG_OK;
     if (!x || !counts) return set_error(SLG_ERR_ARG, "slg_groupsum: null pointer");
-    const int64_t nw32 = cdiv(B, 32);
-    dim3 grid((unsigned)cdiv(nw32, HB_THREADS), (unsigned)num_classes);
-    groupsum_kernel<<<grid, HB_THREADS, 0, as_stream(stream)>>>(
-        reinterpret_cast<const uint32_t*>(x), G, ldw * 2, B, num_classes, counts);
+    dim3 grid((unsigned)cdiv(B, 1024), (unsigned)num_classes);
+    const int64_t per = cdiv(G, GS_SEG);   // rows per segment -> counter planes needed
+    auto xs = reinterpret_cast<const uint32_t*>(x);
+    cudaStream_t st = as_stream(stream);
+    if (per < (1 << 8)) groupsum_kernel<8><<<grid, 256, 0, st>>>(xs, G, ldw * 2, B, num_classes, counts);
+    else if (per < (1 << 12)) groupsum_kernel<12><<<grid, 256, 0, st>>>(xs, G, ldw * 2, B, num_classes, counts);
+    else groupsum_kernel<17><<<grid, 256, 0, st>>>(xs, G, ldw * 2, B, num_classes, counts);
     return check_launch("slg_groupsum");
 }

@@ -50,6 +50,45 @@ pack_kernel(const T* __restrict__ x, int64_t B, int64_t F, uint64_t* __restrict_
     if (myf >= 0 && f0 + myf < F) out[(f0 + myf) * ldw + w] = mine;
 }
 
+// Same tile as pack_kernel, loaded with 16-byte vectors (rows must start on
+// 16-byte boundaries: F * sizeof(T) % 16 == 0 and x 16-byte aligned).
+template <typename T, typename Pred>
+__global__ void __launch_bounds__(PK_THREADS)
+pack_vec_kernel(const T* __restrict__ x, int64_t B, int64_t F, uint64_t* __restrict__ out, int64_t ldw) {
+    constexpr int EPV = 16 / sizeof(T);            // elements per 16-byte vector
+    constexpr int VPR = PK_FT / EPV;               // vectors per tile row
+    __shared__ uint8_t tile[64][PK_FT + 4];
+    const int64_t w = blockIdx.y;
+    const int64_t f0 = (int64_t)blockIdx.x * PK_FT;
+    const int64_t b0 = w * 64;
+    Pred pred;
+    for (int i = threadIdx.x; i < 64 * VPR; i += PK_THREADS) {
+        const int s = i / VPR, q = i % VPR;
+        const int64_t b = b0 + s, ff = f0 + q * EPV;
+        T v[EPV];
+        if (b < B && ff + EPV <= F) {
+            *reinterpret_cast<uint4*>(v) = __ldg(reinterpret_cast<const uint4*>(x + b * F + ff));
+        } else {
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) v[e] = (b < B && ff + e < F) ? x[b * F + ff + e] : T(0);
+        }
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) tile[s][q * EPV + e] = pred(v[e]) ? 1 : 0;
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint64_t mine = 0;
+    int myf = -1;
+#pragma unroll 4
+    for (int j = 0; j < PK_FT / (PK_THREADS / 32); ++j) {
+        int f = warp * (PK_FT / (PK_THREADS / 32)) + j;
+        uint32_t lo = __ballot_sync(0xffffffffu, tile[lane][f]);
+        uint32_t hi = __ballot_sync(0xffffffffu, tile[32 + lane][f]);
+        if (lane == j) { mine = ((uint64_t)hi << 32) | lo; myf = f; }
+    }
+    if (myf >= 0 && f0 + myf < F) out[(f0 + myf) * ldw + w] = mine;
+}
+
 // zero the padding words [nw_valid, ldw) of every row
 __global__ void zero_tail_kernel(uint64_t* out, int64_t rows, int64_t ldw, int64_t nw_valid) {
     int64_t tail = ldw - nw_valid;
@@ -120,7 +159,10 @@ static int launch_pack(const T* x, int64_t B, int64_t F, uint64_t* out, int64_t 
     if (!x || !out) return set_error(SLG_ERR_ARG, "%s: null pointer", name);
     if (nw > 65535) return set_error(SLG_ERR_ARG, "%s: batch too large (%lld words)", name, (long long)nw);
     dim3 grid((unsigned)cdiv(F, PK_FT), (unsigned)nw);
-    pack_kernel<T, Pred><<<grid, PK_THREADS, 0, as_stream(stream)>>>(x, B, F, out, ldw);
+    if ((F * (int64_t)sizeof(T)) % 16 == 0 && aligned16(x))
+        pack_vec_kernel<T, Pred><<<grid, PK_THREADS, 0, as_stream(stream)>>>(x, B, F, out, ldw);
+    else
+        pack_kernel<T, Pred><<<grid, PK_THREADS, 0, as_stream(stream)>>>(x, B, F, out, ldw);
     if (ldw > nw) {
         int64_t n = F * (ldw - nw);
         zero_tail_kernel<<<(unsigned)cdiv(n, 256), 256, 0, as_stream(stream)>>>(out, F, ldw, nw);

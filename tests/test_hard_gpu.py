@@ -152,3 +152,21 @@ def test_learned_thermometer_hard_vs_oracle():
     got = enc.cuda().forward_hard(x.cuda()).cpu().numpy()
     ref = OH.learned_thermometer_bits(x.numpy(), enc.thresholds.detach().cpu().numpy())
     np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.parametrize("B,W,C", [(1, 10, 10), (70, 40000, 2), (3000, 1280, 10), (1025, 60, 3)])
+def test_groupsum_shapes_vs_oracle(B, W, C):
+    from silogic_b200 import _hard
+    x = torch.rand(B, W, generator=torch.Generator().manual_seed(B)) < 0.5
+    c = _hard.groupsum(_hard.pack(x.cuda()), B, C).cpu().numpy()
+    np.testing.assert_array_equal(c, OH.group_sum_counts(OH.pack_bits(x.numpy()), B, C))
+
+
+@pytest.mark.parametrize("F", [1, 15, 16, 33, 784])
+def test_pack_widths_u8_f32_vs_oracle(F):
+    from silogic_b200 import _hard
+    x = torch.rand(131, F, generator=torch.Generator().manual_seed(F)) < 0.4
+    ref = OH.pack_bits(x.numpy())
+    for t in (x.to(torch.uint8), x.float()):
+        got = _hard.pack(t.cuda())[:, :ref.shape[1]].cpu().numpy().view(np.uint64)
+        np.testing.assert_array_equal(got, ref)
