@@ -1,19 +1,27 @@
 """Benchmark of the silogic_b200 hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c1|c3|c4|c5] [--no-soft]
+                    [--config c1|c2|c3|c4|c5] [--no-soft] [--cpu-sample S]
 
-Workload (default): FC LogicNet 784 -> 10000 x 6, Walsh nodes,
-Top-K (k=8) wiring, GroupSum 10 classes tau=10, every parameter N(0,1) (seeded),
-inputs Bernoulli(0.3) (seeded, synthetic).
-  * headline step = hard bit-packed inference of 65,536 samples per GPU
-    (pack -> 6 FC layers -> popcount GroupSum);
-  * "soft" = soft forward + backward of 4,096 samples per GPU (+ one NCCL
-    all-reduce of the parameter gradients when N > 1).
-Timing: CUDA events around each step on the launching stream, L2 flushed (a
-256 MB write) between steps, W warm-up steps; barrier + synchronize around the
-timed loop; the max over ranks is reported.  e2e = the same work through the
-public API from pinned host memory (H2D of the uint8 batch, D2H of the logits)
+Configs are BASELINE.json's (synthetic, seeded inputs; every parameter N(0,1)):
+  c1  FC LogicNet 784 -> 8000 x 4, gate16, fixed wiring; hard + soft at B=1024
+  c2  FC LogicNet 784 -> 10000 x 6, Walsh, Top-K 8 (default, the headline);
+      hard bit-packed inference at B=65,536, soft fwd+bwd at B=4,096
+  c3  LogicTreeNet 3x32x32 thermometer (5 thresholds) -> gate16 trees depth 2,
+      channels 128/256/512 + OR-pool, head 1280; B=4,096
+  c4  LogicConvNet, learned thermometer (3 bits), multilinear arity-6 trees,
+      channels 128/256, head 16000 x 2, STE selection; B=8,192
+  c5  LogicTreeNet 3x32x32 thermometer (31 thresholds), gate16 depth 2, channels
+      1024/2048/4096/8192, head 12800/6400/3200; 1,048,576 samples split across the
+      GPUs (strong scaling), processed in 131,072-sample device chunks
+A "step" is one pass of the hard circuit over the per-GPU batch (value); the
+soft fwd+bwd leg (key "soft_fwd_bwd") is one forward + backward of its batch,
+plus one NCCL all-reduce of the parameter gradients when N > 1.  Hard inference
+shards the batch and all-gathers only the class counts.
+Timing: CUDA events on the launching stream around each step, L2 flushed (a
+256 MB write, untimed) before each step, W >= 3 warm-up steps, barrier +
+synchronize around the timed loop, max over ranks.  "e2e" runs the same work
+through the public API from pinned host memory with the host<->device copies
 inside the timed region.
 """
 import argparse
@@ -31,24 +39,44 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+FIVE = [1 / 6, 2 / 6, 3 / 6, 4 / 6, 5 / 6]
+THIRTY_ONE = [(i + 1) / 32 for i in range(31)]
+
 CONFIGS = {
-    "c2": dict(ctor="LogicNet", kwargs=dict(in_dim=784, width=10000, depth=6, node="walsh",
-                                             connectome="topk", k=8, tau=10.0, seed=0),
-               hard_batch=65536, soft_batch=4096,
-               name="C2 FC LogicNet 784->10000x6 walsh topk8 GroupSum10 tau10"),
-    "c1": dict(ctor="LogicNet", kwargs=dict(in_dim=784, width=8000, depth=4, node="gate16",
-                                             connectome="fixed", tau=10.0, seed=0),
-               hard_batch=1024, soft_batch=1024,
+    "c1": dict(ctor="LogicNet", inp="bern",
+               kwargs=dict(in_dim=784, width=8000, depth=4, node="gate16", connectome="fixed",
+                           tau=10.0, seed=0),
+               hard_batch=1024, soft_batch=1024, scaling="weak",
                name="C1 FC LogicNet 784->8000x4 gate16 fixed GroupSum10 tau10"),
+    "c2": dict(ctor="LogicNet", inp="bern",
+               kwargs=dict(in_dim=784, width=10000, depth=6, node="walsh", connectome="topk", k=8,
+                           tau=10.0, seed=0),
+               hard_batch=65536, soft_batch=4096, scaling="weak",
+               name="C2 FC LogicNet 784->10000x6 walsh topk8 GroupSum10 tau10"),
+    "c3": dict(ctor="LogicTreeNet", inp="image", thresholds=FIVE,
+               kwargs=dict(in_channels=15, in_hw=32, channels=[128, 256, 512], head_widths=[1280],
+                           tree_depth=2, node="gate16", tau=20.0, seed=0),
+               hard_batch=4096, soft_batch=4096, scaling="weak",
+               name="C3 LogicTreeNet 3x32x32 thermo5 gate16 d2 [128,256,512]+OrPool head1280"),
+    "c4": dict(ctor="LogicConvNet", inp="encoder", bits=3,
+               kwargs=dict(in_channels=9, in_hw=32, channels=[128, 256], head_widths=[16000, 16000],
+                           tree_depth=1, node="multilinear", arity=6, connect="topk", k=8, n_chan=4,
+                           gate_select="hard", tau=12.0, seed=0),
+               hard_batch=8192, soft_batch=8192, scaling="weak",
+               name="C4 LogicConvNet learned-thermo3 multilinear a6 d1 [128,256] head 16000x2"),
+    "c5": dict(ctor="LogicTreeNet", inp="image", thresholds=THIRTY_ONE,
+               kwargs=dict(in_channels=93, in_hw=32, channels=[1024, 2048, 4096, 8192],
+                           head_widths=[12800, 6400, 3200], head_connect="F", tree_depth=2,
+                           node="gate16", tau=20.0, seed=0),
+               hard_batch=1048576, soft_batch=0, scaling="strong", chunk=131072,
+               name="C5 LogicTreeNet 3x32x32 thermo31 gate16 d2 [1024..8192] head 12800/6400/3200"),
 }
 
 
 # ------------------------------------------------------------------ helpers
 def dist_env():
-    ws = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return ws, rank, local
+    return (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+            int(os.environ.get("LOCAL_RANK", "0")))
 
 
 def build_model(cfg, seed=0):
@@ -59,17 +87,22 @@ def build_model(cfg, seed=0):
     with torch.no_grad():
         for p in m.parameters():
             p.copy_(torch.randn(p.shape, generator=g))
-    return m
+    enc = None
+    if cfg["inp"] == "encoder":
+        enc = S.LearnedThermometerEncoder(3 * 32 * 32, cfg["bits"])
+    return m, enc
 
 
 def make_input(cfg, B, seed):
+    """Synthetic batch: Bernoulli(0.3) features (uint8) or U[0,1] 3x32x32 pixels (fp32)."""
     g = torch.Generator().manual_seed(seed)
-    F = cfg["kwargs"]["in_dim"]
-    return (torch.rand(B, F, generator=g) < 0.3).to(torch.uint8)
+    if cfg["inp"] == "bern":
+        return (torch.rand(B, cfg["kwargs"]["in_dim"], generator=g) < 0.3).to(torch.uint8)
+    return torch.rand(B, 3, 32, 32, generator=g)
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons every 200 ms during the timed region."""
 
     Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -102,8 +135,9 @@ class ClockSampler:
     def summary(self):
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
-        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        num = lambda s: s.replace(".", "", 1).isdigit()
+        sm = [float(r[0]) for r in self.rows if num(r[0])]
+        mx = [float(r[1]) for r in self.rows if num(r[1])]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in self.rows for i in range(4)
                           if len(r) > 3 + i and r[3 + i].lower() == "active"})
@@ -115,71 +149,144 @@ def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
-            d = json.load(f)
-        return float(d["hbm_gbs"]), "measured"
+            return float(json.load(f)["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
 
 
+def events():
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+# ------------------------------------------------------- algorithmic bytes
+def hard_stage_bytes(cfg, plan):
+    """Layer-wise algorithmic bytes PER SAMPLE of each hard stage: every stage reads its
+    input bits once and writes its output bits once; the first stage reads the raw
+    input (uint8 features, or fp32 pixels for the image configs)."""
+    out = []
+    if cfg["inp"] == "bern":
+        F = cfg["kwargs"]["in_dim"]
+        out.append(("pack", F + F / 8))
+        bits = F
+    else:
+        T = len(cfg["thresholds"]) if cfg["inp"] == "image" else cfg["bits"]
+        out.append(("pack", 3 * 32 * 32 * 4 + 3 * T * 32 * 32 / 8))
+        bits, hw = 3 * T * 32 * 32, 32
+    for st in plan.steps:
+        if st["op"] == "fc":
+            o = st["idx"].shape[0]
+            out.append(("fc_hard", (bits + o) / 8))
+            bits = o
+        else:
+            hw //= st["pool"]
+            o = st["n"] * hw * hw
+            out.append(("conv_hard", (bits + o) / 8))
+            bits = o
+    out.append(("groupsum", bits / 8 + 40))
+    return out
+
+
+def soft_bytes_per_sample(cfg, model):
+    """Layer-wise fp32 bytes per sample of soft fwd+bwd: fwd (in + out) * 4 per layer,
+    bwd (out + in + in) * 4 (the data input needs no gradient; the learned encoder's
+    does), conv blocks count their pooled output, GroupSum 4W + 40 each way."""
+    from silogic_b200.layers import ConvLogicTree
+    if cfg["ctor"] == "LogicNet":
+        dims = [cfg["kwargs"]["in_dim"]] + [L.out_dim for L in model.layers]
+    else:
+        hw = cfg["kwargs"]["in_hw"]
+        dims = [cfg["kwargs"]["in_channels"] * hw * hw]
+        for b in model.blocks:
+            if isinstance(b, ConvLogicTree):
+                hw //= 2
+                dims.append(b.n * hw * hw)
+        dims += [L.out_dim for L in model.head_layers]
+    first_grad = cfg["inp"] == "encoder"
+    fwd = sum((a + b) * 4 for a, b in zip(dims[:-1], dims[1:]))
+    bwd = sum((b + a + (a if (i > 0 or first_grad) else 0)) * 4
+              for i, (a, b) in enumerate(zip(dims[:-1], dims[1:])))
+    return fwd + bwd + 2 * (4 * dims[-1] + 40)
+
+
 # ------------------------------------------------------------------ hard leg
-class KernelTimer:
-    """CUDA events around launches of one kernel on the current stream."""
-
-    def __init__(self):
-        self.pairs = []
-
-    def start(self):
-        e = torch.cuda.Event(enable_timing=True)
-        e.record()
-        return e
-
-    def stop(self, e0):
-        e1 = torch.cuda.Event(enable_timing=True)
-        e1.record()
-        self.pairs.append((e0, e1))
-
-    def mean_ms(self):
-        return statistics.mean(a.elapsed_time(b) for a, b in self.pairs) if self.pairs else None
-
-
 def run_hard(cfg, B, steps, warmup, rank, ws, dev):
     from silogic_b200 import _hard
-    from silogic_b200.bitpacking import convert_logic_net
+    from silogic_b200.bitpacking import convert_logic_net, convert_logic_conv_net
     from silogic_b200.bitpacking.plan import HardPlan
-    model = build_model(cfg).to(dev)
+    model, enc = build_model(cfg)
+    model = model.to(dev)
     plan = HardPlan.from_model(model)
-    bp = convert_logic_net(model)
-    x_host = make_input(cfg, B, seed=1 + rank).pin_memory()
+    bp = convert_logic_net(model) if cfg["ctor"] == "LogicNet" else convert_logic_conv_net(model)
+    chunk = min(B, cfg.get("chunk", B))
+    x_host = make_input(cfg, chunk, seed=1 + rank).pin_memory()
     x_dev = x_host.to(dev)
+    thr = None
+    if cfg["inp"] == "image":
+        thr = torch.tensor(cfg["thresholds"], dtype=torch.float32, device=dev)
+    elif cfg["inp"] == "encoder":
+        thr = enc.thresholds.detach().to(dev).contiguous()
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.int32, device=dev)   # 256 MB > L2
-    in_dim, width = cfg["kwargs"]["in_dim"], cfg["kwargs"]["width"]
-    fc_timer = KernelTimer()
+    timers = {}
     launches = [0]
+    nchunks = (B + chunk - 1) // chunk
+    counts_all = torch.empty((B, plan.num_classes), dtype=torch.int32, device=dev)
+    gathered = torch.empty((ws * B, plan.num_classes), dtype=torch.int32, device=dev) if ws > 1 else None
+    mode = 0 if cfg["inp"] == "image" else 1
 
-    def step_device():
-        h = plan.pack_input(x_dev)
-        launches[0] += 1
-        for i, st in enumerate(plan.steps):
-            t0 = fc_timer.start() if i > 0 else None
-            h = _hard.fc(h, st["idx"], st["tt"], st["wire_r"])
-            if t0 is not None:
-                fc_timer.stop(t0)
+    def pack_chunk(n):
+        if cfg["inp"] == "bern":
+            return plan.pack_input(x_dev[:n])
+        return _hard.thermo_pack(x_dev[:n], thr, mode=mode)
+
+    def timed(name, fn, record):
+        if not record:
+            return fn()
+        e0, e1 = events()
+        e0.record()
+        r = fn()
+        e1.record()
+        timers.setdefault(name, []).append((e0, e1))
+        return r
+
+    def step_device(record=False):
+        for c in range(nchunks):
+            n = min(chunk, B - c * chunk)
+            h = timed("pack", lambda: pack_chunk(n), record)
             launches[0] += 1
-        c = _hard.groupsum(h, B, plan.num_classes)
-        launches[0] += 1
-        return c
+            for st in plan.steps:
+                hh = h
+                if st["op"] == "fc":
+                    hh = h.reshape(-1, h.shape[-1])
+                    h = timed("fc_hard", lambda: _hard.fc(hh, st["idx"], st["tt"], st["wire_r"]), record)
+                else:
+                    h = timed("conv_hard", lambda: _hard.conv(hh, st["leaf"], st["tt"], st["arity"],
+                                                              st["depth"], st["kernel"], st["pad"],
+                                                              st["wire_r"], st["pool"]), record)
+                launches[0] += 1
+            hh = h.reshape(-1, h.shape[-1])
+            timed("groupsum", lambda: _hard.groupsum(hh, n, plan.num_classes,
+                                                      out=counts_all[c * chunk:c * chunk + n]), record)
+            launches[0] += 1
+        if ws > 1:   # only the class counts leave the GPU
+            torch.distributed.all_gather_into_tensor(gathered, counts_all)
+        return counts_all
 
     def step_e2e():
-        # public API: host uint8 in (pinned), logits out to host
-        out = bp.forward(x_host.to(dev, non_blocking=True))
-        return out.to("cpu", non_blocking=True)
+        outs = []
+        for c in range(nchunks):
+            n = min(chunk, B - c * chunk)
+            xd = x_host[:n].to(dev, non_blocking=True)
+            if cfg["inp"] == "bern":
+                outs.append(bp.forward(xd).to("cpu", non_blocking=True))
+            else:
+                outs.append(bp.forward_images(xd, thr, mode=mode).to("cpu", non_blocking=True))
+        return outs
 
-    ref = step_device()
+    step_device()
     torch.cuda.synchronize()
     for _ in range(warmup):
         step_device()
         step_e2e()
     torch.cuda.synchronize()
-    fc_timer.pairs.clear()
     launches[0] = 0
     if ws > 1:
         torch.distributed.barrier()
@@ -189,10 +296,9 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
         torch.cuda.nvtx.range_push("timed_hard")
         for _ in range(steps):
             flush.fill_(1)
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
+            e0, e1 = events()
             e0.record()
-            step_device()
+            step_device(record=True)
             e1.record()
             times.append((e0, e1))
         torch.cuda.synchronize()
@@ -201,10 +307,9 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
         e2e_times = []
         for _ in range(steps):
             flush.fill_(1)
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
+            e0, e1 = events()
             e0.record()
-            out = step_e2e()
+            step_e2e()
             e1.record()
             e1.synchronize()
             e2e_times.append(e0.elapsed_time(e1))
@@ -212,40 +317,42 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
     if ws > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    fc_ms = fc_timer.mean_ms()
-    nw = (B + 63) // 64
-    return dict(ms=ms, e2e_ms=e2e_ms, fc_ms=fc_ms, launches_per_step=launches[0] / steps,
-                clocks=clk.summary(), counts=ref,
-                h2d=int(x_host.numel()), d2h=int(B * plan.num_classes * 4),
-                fc_bytes=(width + width) * nw * 8)
+    kern = {k: (sum(a.elapsed_time(b) for a, b in v) / steps, len(v) / steps) for k, v in timers.items()}
+    stage = hard_stage_bytes(cfg, plan)
+    per_kind = {}
+    for name, bps in stage:
+        per_kind[name] = per_kind.get(name, 0.0) + bps
+    in_bytes = x_host[:1].numel() * x_host.element_size()
+    return dict(ms=ms, e2e_ms=e2e_ms, kern=kern, per_kind=per_kind,
+                bytes_per_sample=sum(b for _, b in stage), launches_per_step=launches[0] / steps,
+                clocks=clk.summary(), h2d=int(in_bytes * B), d2h=int(B * plan.num_classes * 4))
 
 
 # ------------------------------------------------------------------ soft leg
-def soft_bytes_per_sample(cfg):
-    """Layer-wise algorithmic fp32 bytes per sample of soft fwd+bwd (each stage reads its
-    inputs once and writes its outputs once; the data input needs no gradient)."""
-    kw = cfg["kwargs"]
-    dims = [kw["in_dim"]] + [kw["width"]] * kw["depth"]
-    fwd = sum((a + b) * 4 for a, b in zip(dims[:-1], dims[1:]))
-    bwd = sum((b + a + (a if i > 0 else 0)) * 4 for i, (a, b) in enumerate(zip(dims[:-1], dims[1:])))
-    W = dims[-1]
-    return fwd + bwd + (4 * W + 40) * 2
-
-
 def run_soft(cfg, B, steps, warmup, rank, ws, dev):
-    model = build_model(cfg).to(dev).train()
-    x = make_input(cfg, B, seed=100 + rank).float().to(dev)
-    g = torch.Generator().manual_seed(5)
-    rmat = torch.randn(B, 10, generator=g).to(dev)
+    import silogic_b200 as S
+    model, enc = build_model(cfg)
+    model = model.to(dev).train()
+    if enc is not None:
+        enc = enc.to(dev)
+    x = make_input(cfg, B, seed=100 + rank).to(dev)
+    if cfg["inp"] == "bern":
+        x = x.float()
+    elif cfg["inp"] == "image":
+        x = S.binarize_spatial(x, cfg["thresholds"]).float()
+    else:
+        x = x.reshape(B, -1)
+    rmat = torch.randn(B, 10, generator=torch.Generator().manual_seed(5)).to(dev)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.int32, device=dev)
-    params = [p for p in model.parameters()]
-    bucket = None
+    params = list(model.parameters()) + (list(enc.parameters()) if enc is not None else [])
 
     def step():
-        nonlocal bucket
         for p in params:
             p.grad = None
-        logits = model(x)
+        xi = x
+        if enc is not None:
+            xi = enc(x).view(B, 3, 32, 32, cfg["bits"]).permute(0, 1, 4, 2, 3).reshape(B, -1, 32, 32)
+        logits = model(xi)
         (logits * rmat).sum().backward()
         if ws > 1:      # data parallel: one all-reduce of every parameter gradient
             bucket = torch.cat([p.grad.reshape(-1) for p in params])
@@ -261,16 +368,15 @@ def run_soft(cfg, B, steps, warmup, rank, ws, dev):
     torch.cuda.nvtx.range_push("timed_soft")
     for _ in range(steps):
         flush.fill_(1)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
+        e0, e1 = events()
         e0.record()
         step()
         e1.record()
         times.append((e0, e1))
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_pop()
-    ms = statistics.mean(a.elapsed_time(b) for a, b in times)
-    return dict(ms=ms)
+    return dict(ms=statistics.mean(a.elapsed_time(b) for a, b in times),
+                bytes_per_sample=soft_bytes_per_sample(cfg, model))
 
 
 # ------------------------------------------------------------ CPU baselines
@@ -278,16 +384,24 @@ _SPEC_CACHE = {}
 
 
 def cpu_hard_sample(cfg, n_samples, threads=1):
-    """Oracle (numpy bit-packed restatement of the reference) on a bounded sample."""
+    """The CPU oracle (numpy bit-packed restatement of the reference's hard path) on a
+    bounded sample: ``threads`` workers over 64-sample-aligned slices."""
     from concurrent.futures import ThreadPoolExecutor
     from oracle import hard as OH
     from oracle.spec import net_spec
-    key = cfg["name"]
+    key = (cfg["name"], n_samples)
     if key not in _SPEC_CACHE:
-        model = build_model(cfg)
+        model, enc = build_model(cfg)
         sd = {k: v.numpy() for k, v in model.state_dict().items()}
-        _SPEC_CACHE[key] = (net_spec(cfg["ctor"], cfg["kwargs"], sd),
-                            make_input(cfg, n_samples, seed=1).numpy())
+        spec = net_spec(cfg["ctor"], cfg["kwargs"], sd)
+        x = make_input(cfg, n_samples, seed=1).numpy()
+        if cfg["inp"] == "image":
+            x = OH.thermometer_bits(x, cfg["thresholds"])
+        elif cfg["inp"] == "encoder":
+            e = OH.learned_thermometer_bits(x.reshape(n_samples, -1), enc.thresholds.detach().numpy())
+            x = e.reshape(n_samples, 3, 32, 32, cfg["bits"]).transpose(0, 1, 4, 2, 3).reshape(
+                n_samples, -1, 32, 32)
+        _SPEC_CACHE[key] = (spec, x)
     spec, x = _SPEC_CACHE[key]
     chunk = max(64, (n_samples // threads) // 64 * 64)
     parts = [x[i:i + chunk] for i in range(0, n_samples, chunk)]
@@ -298,6 +412,9 @@ def cpu_hard_sample(cfg, n_samples, threads=1):
     return n_samples / dt, dt
 
 
+DEFAULT_CPU_SAMPLE = {"c1": 1024, "c2": 4096, "c3": 256, "c4": 128, "c5": 64}
+
+
 # ------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -306,84 +423,89 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
-    ap.add_argument("--cpu-sample", type=int, default=4096)
+    ap.add_argument("--cpu-sample", type=int, default=None)
     ap.add_argument("--no-soft", action="store_true")
     a = ap.parse_args()
     cfg = CONFIGS[a.config]
     ws, rank, local = dist_env()
     warmup = max(3, a.warmup)
     metric = "hard-circuit samples/s (bit-packed inference)"
+    cpu_n = a.cpu_sample or DEFAULT_CPU_SAMPLE[a.config]
 
     if a.impl == "reference":
         if rank != 0:
             return
         threads = os.cpu_count() or 1
-        vals = []
-        for _ in range(warmup):
-            cpu_hard_sample(cfg, a.cpu_sample, threads)
-        for _ in range(a.steps):
-            v, _ = cpu_hard_sample(cfg, a.cpu_sample, threads)
-            vals.append(v)
+        n = cpu_n * 4 if a.config in ("c1", "c2") else cpu_n
+        cpu_hard_sample(cfg, n, threads)
+        vals = [cpu_hard_sample(cfg, n, threads)[0] for _ in range(a.steps)]
         v = statistics.mean(vals)
-        line = {"metric": metric, "value": v, "unit": "samples/s", "n_gpus": a.gpus,
-                "steps": a.steps, "warmup": warmup, "ms_per_step": a.cpu_sample / v * 1e3,
-                "higher_is_better": True, "impl": "reference", "dtype": "u64",
-                "data": "synthetic", "config": {"workload": cfg["name"], "batch": a.cpu_sample},
-                "cpu_baseline": {"value": v, "unit": "samples/s", "cores": threads, "kind": "port",
-                                 "sample": f"{a.cpu_sample} samples per step, numpy bit-packed "
-                                           f"restatement of the reference, {threads} threads"},
-                "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0}}
-        print(json.dumps(line))
+        print(json.dumps({
+            "metric": metric, "value": v, "unit": "samples/s", "n_gpus": ws, "steps": a.steps,
+            "warmup": warmup, "ms_per_step": n / v * 1e3, "higher_is_better": True,
+            "impl": "reference", "dtype": "u64", "data": "synthetic",
+            "config": {"workload": cfg["name"], "batch": n},
+            "cpu_baseline": {"value": v, "unit": "samples/s", "cores": threads, "kind": "port",
+                             "sample": f"{n} samples per step through the numpy bit-packed "
+                                       f"restatement of the reference, {threads} threads"},
+            "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}))
         return
 
     if ws > 1:
         torch.distributed.init_process_group("nccl")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    B = cfg["hard_batch"]
+    B = cfg["hard_batch"] // (ws if cfg["scaling"] == "strong" else 1)
     r = run_hard(cfg, B, a.steps, warmup, rank, ws, dev)
     soft = None
-    if not a.no_soft:
+    if not a.no_soft and cfg["soft_batch"]:
         soft = run_soft(cfg, cfg["soft_batch"], a.steps, warmup, rank, ws, dev)
     ms = torch.tensor([r["ms"], r["e2e_ms"], soft["ms"] if soft else 0.0], device=dev)
     if ws > 1:
         torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
     ms_step, e2e_ms, soft_ms = ms.tolist()
     hbm, kind = peaks()
-    fc_gbs = r["fc_bytes"] / (r["fc_ms"] * 1e-3) / 1e9
     if rank == 0:
+        # dominant kernel kind and its achieved bandwidth (algorithmic bytes / launch time)
+        dom = max(r["kern"], key=lambda k: r["kern"][k][0])
+        dom_ms, dom_n = r["kern"][dom]
+        dom_bytes = r["per_kind"][dom] * B
+        ach = dom_bytes / (dom_ms * 1e-3) / 1e9
+        total = B * ws if cfg["scaling"] == "weak" else cfg["hard_batch"]
         line = {
-            "metric": metric, "value": B * ws / (ms_step * 1e-3), "unit": "samples/s",
-            "n_gpus": ws, "steps": a.steps, "warmup": warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u64",
-            "data": "synthetic (Bernoulli(0.3) inputs, N(0,1) parameters, seeded)",
-            "config": {"workload": cfg["name"], "batch_per_gpu": B, "global_batch": B * ws,
-                       "parallelism": f"batch-shard x{ws}", "l2": "flushed (256 MB write) between steps"},
-            "e2e": {"value": B * ws / (e2e_ms * 1e-3), "unit": "samples/s",
+            "metric": metric, "value": total / (ms_step * 1e-3), "unit": "samples/s", "n_gpus": ws,
+            "steps": a.steps, "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": cfg["scaling"], "vs_baseline": None, "dtype": "u64",
+            "data": "synthetic (seeded inputs, N(0,1) parameters)",
+            "config": {"workload": cfg["name"], "batch_per_gpu": B, "global_batch": total,
+                       "parallelism": f"batch shard x{ws}, counts all-gathered",
+                       "l2": "flushed (256 MB write) before each step"},
+            "e2e": {"value": total / (e2e_ms * 1e-3), "unit": "samples/s",
                     "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
             "gpu_launches": int(round(r["launches_per_step"] * a.steps)),
-            "roofline": {"kernel": "slg_fc_hard (layers 2-6)", "bound": "hbm",
-                         "achieved": fc_gbs, "peak": hbm, "unit": "GB/s", "frac": fc_gbs / hbm,
+            "roofline": {"kernel": f"slg_{dom} ({dom_n:.0f} launches/step)", "bound": "hbm",
+                         "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
                          "peak_kind": kind, "traffic": None,
-                         "algorithmic_bytes_per_launch": r["fc_bytes"]},
+                         "algorithmic_bytes_per_step": dom_bytes,
+                         "step_frac": r["bytes_per_sample"] * B / (ms_step * 1e-3) / 1e9 / hbm},
+            "kernels_ms_per_step": {k: v[0] for k, v in r["kern"].items()},
             "clocks": r["clocks"],
         }
         if soft:
             Bs = cfg["soft_batch"]
-            bps = soft_bytes_per_sample(cfg)
-            ach = bps * Bs / (soft_ms * 1e-3) / 1e9
+            ach_s = soft["bytes_per_sample"] * Bs / (soft_ms * 1e-3) / 1e9
             line["soft_fwd_bwd"] = {
                 "metric": "soft fwd+bwd samples/s", "value": Bs * ws / (soft_ms * 1e-3),
                 "unit": "samples/s", "ms_per_step": soft_ms, "batch_per_gpu": Bs, "dtype": "f32",
-                "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
-                             "frac": ach / hbm, "algorithmic_bytes_per_sample": bps,
-                             "scope": "whole step (layer-wise bytes)"},
+                "roofline": {"bound": "hbm (layer-wise bytes; gathers are L2-bound)",
+                             "achieved": ach_s, "peak": hbm, "unit": "GB/s", "frac": ach_s / hbm,
+                             "algorithmic_bytes_per_sample": soft["bytes_per_sample"]},
                 "collective": "one NCCL all-reduce of all parameter gradients" if ws > 1 else None}
         if ws == 1:
-            v, dt = cpu_hard_sample(cfg, a.cpu_sample, 1)
+            v, dt = cpu_hard_sample(cfg, cpu_n, 1)
             line["cpu_baseline"] = {"value": v, "unit": "samples/s", "cores": 1, "kind": "port",
-                                    "sample": f"{a.cpu_sample} samples, numpy bit-packed "
+                                    "sample": f"{cpu_n} samples through the numpy bit-packed "
                                               f"restatement of the reference ({dt:.2f} s)"}
         print(json.dumps(line))
     if ws > 1:

@@ -143,6 +143,17 @@ class BitpackedNet:
 class BitpackedConvNet(BitpackedNet):
     """End-to-end bit-packed ``LogicConvNet``: ``[B, C, H, W]`` uint8 -> logits."""
 
+    def forward_images(self, img, thresholds, mode=0):
+        """Logits from real-valued images ``[B, C, H, W]`` with the thermometer encoding
+        fused into the packing kernel (never materialising the bit planes as bytes).
+        ``mode`` 0: shared ``thresholds`` [T] as in ``binarize_spatial``; 1: per-feature
+        learned thresholds ``[C*H*W, T]`` as in ``LearnedThermometerEncoder``."""
+        was_np = isinstance(img, np.ndarray)
+        t = _as_cuda(img)
+        h = _hard.thermo_pack(t, thresholds, mode=mode)
+        logits = self.plan.counts_from_packed(h, t.shape[0]).float() / self.head.tau
+        return logits.cpu().numpy() if was_np else logits
+
     @classmethod
     def from_conv_net(cls, bp_conv_net, H_in=None, W_in=None, device="cuda"):
         """Reference ``BitpackedConvGPUNet.from_conv_net`` signature: the net is already

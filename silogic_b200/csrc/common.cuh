@@ -48,6 +48,30 @@ __device__ __forceinline__ uint32_t lut_eval(const uint32_t (&v)[AR], uint64_t t
     return f[0];
 }
 
+// Same evaluation with the 2^AR leaf masks precomputed (m[p] = all-ones iff bit p
+// of the table is set); the masks depend only on the node, so a thread that
+// evaluates several words of one node builds them once.
+template <int AR>
+__device__ __forceinline__ void lut_masks(uint64_t tt, uint32_t (&m)[1 << AR]) {
+#pragma unroll
+    for (int p = 0; p < (1 << AR); ++p) m[p] = tt_mask(tt, p);
+}
+
+template <int AR>
+__device__ __forceinline__ uint32_t lut_eval_m(const uint32_t (&v)[AR], const uint32_t (&m)[1 << AR]) {
+    constexpr int P = 1 << AR;
+    uint32_t f[P / 2];
+#pragma unroll
+    for (int q = 0; q < P / 2; ++q) f[q] = (v[0] & m[2 * q + 1]) | (~v[0] & m[2 * q]);
+#pragma unroll
+    for (int j = 1; j < AR; ++j) {
+#pragma unroll
+        for (int q = 0; q < (P >> (j + 1)); ++q)
+            f[q] = (v[j] & f[2 * q + 1]) | (~v[j] & f[2 * q]);
+    }
+    return f[0];
+}
+
 __device__ __forceinline__ uint32_t u4get(const uint4& a, int i) {
     return i == 0 ? a.x : (i == 1 ? a.y : (i == 2 ? a.z : a.w));
 }

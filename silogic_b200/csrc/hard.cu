@@ -38,14 +38,15 @@ fc_hard_kernel(const uint4* __restrict__ x, int64_t nvec, const int32_t* __restr
             const int64_t row = __ldg(&idx[o * AR + j]);
             in[j] = __ldg(&x[row * nvec + v]);
         }
-        const uint64_t t = __ldg(&tt[o]);
+        uint32_t m[1 << AR];
+        lut_masks<AR>(__ldg(&tt[o]), m);
         uint32_t res[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             uint32_t vv[AR];
 #pragma unroll
             for (int j = 0; j < AR; ++j) vv[j] = u4get(in[j], c);
-            res[c] = lut_eval<AR>(vv, t);
+            res[c] = lut_eval_m<AR>(vv, m);
         }
         r = make_uint4(res[0], res[1], res[2], res[3]);
     }
@@ -87,9 +88,14 @@ conv_hard_kernel(const uint4* __restrict__ x, int64_t cin, int H, int W, int64_t
         ly[l] = (r % kk) / kernel - pad;
         lx[l] = r % kernel - pad;
     }
+    constexpr bool PRE = NODES * (1 << AR) <= 64;   // leaf masks of every node fit in registers
     uint64_t tn[NODES];
+    uint32_t mk[PRE ? NODES : 1][1 << AR];
 #pragma unroll
-    for (int i = 0; i < NODES; ++i) tn[i] = __ldg(&tt[n * NODES + i]);
+    for (int i = 0; i < NODES; ++i) {
+        tn[i] = __ldg(&tt[n * NODES + i]);
+        if constexpr (PRE) lut_masks<AR>(tn[i], mk[i]);
+    }
 
     uint4 acc = make_uint4(0, 0, 0, 0);
     for (int oy = 0; oy < pool; ++oy) {
@@ -120,7 +126,8 @@ conv_hard_kernel(const uint4* __restrict__ x, int64_t cin, int H, int W, int64_t
                             uint32_t vv[AR];
 #pragma unroll
                             for (int j = 0; j < AR; ++j) vv[j] = val[m * AR + j][c];
-                            val[m][c] = lut_eval<AR>(vv, tn[node_base + m]);
+                            if constexpr (PRE) val[m][c] = lut_eval_m<AR>(vv, mk[node_base + m]);
+                            else val[m][c] = lut_eval<AR>(vv, tn[node_base + m]);
                         }
                     }
                     node_base += nn;
@@ -157,6 +164,7 @@ groupsum_kernel(const uint32_t* __restrict__ x, int64_t G, int64_t ld32, int64_t
     for (int l = 0; l < LEVELS; ++l) plane[l] = 0;
     if (w * 32 < B) {
         const uint32_t* base = x + (int64_t)c * G * ld32 + w;
+#pragma unroll 4
         for (int64_t g = g0; g < g1; ++g) {
             uint32_t carry = __ldg(base + g * ld32);
 #pragma unroll

@@ -170,3 +170,23 @@ def test_pack_widths_u8_f32_vs_oracle(F):
     for t in (x.to(torch.uint8), x.float()):
         got = _hard.pack(t.cuda())[:, :ref.shape[1]].cpu().numpy().view(np.uint64)
         np.testing.assert_array_equal(got, ref)
+
+
+def test_forward_images_fuses_thermometer_vs_oracle():
+    """BitpackedConvNet.forward_images(img) == oracle counts of binarize_spatial(img)."""
+    import silogic_b200 as S
+    from silogic_b200.bitpacking import convert_logic_conv_net
+    kw = dict(in_channels=15, in_hw=16, channels=[24, 40], head_widths=[160], tree_depth=2,
+              node="gate16", tau=4.0, seed=3)
+    torch.manual_seed(2)
+    m = S.LogicTreeNet(**kw)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.normal_()
+    img = torch.rand(200, 3, 16, 16, generator=torch.Generator().manual_seed(4))
+    sd = {k: v.numpy() for k, v in m.state_dict().items()}
+    th = [1 / 6, 2 / 6, 3 / 6, 4 / 6, 5 / 6]
+    ref = OH.model_counts("LogicTreeNet", kw, sd, OH.thermometer_bits(img.numpy(), th))
+    bp = convert_logic_conv_net(m.cuda())
+    got = bp.forward_images(img.cuda(), th) * 4.0
+    np.testing.assert_array_equal(np.rint(got.cpu().numpy()), ref)
