@@ -221,7 +221,7 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
     x_dev = x_host.to(dev)
     thr = None
     if cfg["inp"] == "image":
-        thr = torch.tensor(cfg["thresholds"], dtype=torch.float32, device=dev)
+        thr = list(cfg["thresholds"])
     elif cfg["inp"] == "encoder":
         thr = enc.thresholds.detach().to(dev).contiguous()
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.int32, device=dev)   # 256 MB > L2
@@ -425,8 +425,13 @@ def main():
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--cpu-sample", type=int, default=None)
     ap.add_argument("--no-soft", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the hard batch (small cases for profiling)")
     a = ap.parse_args()
-    cfg = CONFIGS[a.config]
+    cfg = dict(CONFIGS[a.config])
+    if a.batch:
+        cfg["hard_batch"] = a.batch
+        cfg["chunk"] = min(cfg.get("chunk", a.batch), a.batch)
     ws, rank, local = dist_env()
     warmup = max(3, a.warmup)
     metric = "hard-circuit samples/s (bit-packed inference)"

@@ -64,6 +64,7 @@ int slg_unpack_u8(const uint64_t* p, int64_t F, int64_t ldw, int64_t B, uint8_t*
 /* Thermometer encoding fused with packing.  x is [B, C, HW] fp32.
  * mode 0: binarize_spatial (silogic/data.py:75-92): thr[T] shared, bit = x >= thr[t],
  *         output channel t*C + c.
+ * mode 2: mode 0 with thr sorted ascending (the caller guarantees it): binary search.
  * mode 1: LearnedThermometerEncoder.forward_hard (silogic/encoders.py:46-50):
  *         thr[C*HW, T] per feature, bit = (x - thr[f, t]) > 0, output channel c*T + t.
  * out is [C*T, HW, ldw]. */

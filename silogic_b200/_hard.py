@@ -54,19 +54,44 @@ def unpack(p, B):
     return out
 
 
+_THR_CACHE = {}
+
+
+def _thresholds(thresholds, device):
+    """Shared thresholds as a device tensor (cached for Python sequences) + sortedness."""
+    if isinstance(thresholds, (list, tuple)):
+        key = (tuple(float(t) for t in thresholds), str(device))
+        hit = _THR_CACHE.get(key)
+        if hit is None:
+            vals = [float(t) for t in thresholds]
+            t = torch.tensor(vals, dtype=torch.float32).to(device)
+            hit = (t, all(a <= b for a, b in zip(vals, vals[1:])))
+            _THR_CACHE[key] = hit
+        return hit
+    t = torch.as_tensor(thresholds, dtype=torch.float32, device=device).contiguous()
+    return t, False
+
+
 def thermo_pack(img, thresholds, mode=0, ldw=None):
     """Thermometer-encode ``[B, C, H, W]`` fp32 and pack to ``[C*T, H, W, ldw]``.
 
-    mode 0 = ``binarize_spatial`` (shared thresholds, channel ``t*C + c``);
+    mode 0 = ``binarize_spatial`` (shared thresholds, channel ``t*C + c``; a sorted
+    Python sequence takes the binary-search kernel path);
     mode 1 = learned encoder (per-feature thresholds ``[C*H*W, T]``, channel ``c*T + t``).
     """
     require_cuda(img)
     B, C, H, W = img.shape
-    thr = torch.as_tensor(thresholds, dtype=torch.float32, device=img.device).contiguous()
+    if mode == 0:
+        thr, is_sorted = _thresholds(thresholds, img.device)
+        if is_sorted:
+            mode = 2
+    else:
+        thr = torch.as_tensor(thresholds, dtype=torch.float32, device=img.device).contiguous()
     T = thr.shape[-1] if thr.dim() else 1
     ldw = ldw or ldw_for(B)
     out = torch.empty((C * T, H, W, ldw), dtype=torch.int64, device=img.device)
     x = img.float().contiguous()
+    mode = int(mode)
     call("slg_thermo_pack", ptr(x), B, C, H * W, ptr(thr), T, mode, ptr(out), ldw,
          stream_ptr(img.device))
     return out

@@ -111,7 +111,8 @@ __device__ __forceinline__ float conv_tree_value(const ConvSmem<NODE, AR, D>& S,
         float s = 0.f;
 #pragma unroll
         for (int k = 0; k < KT; ++k) {
-            if (k < K) {
+            // zero weights (one-hot straight-through selection) contribute nothing: skip the load
+            if (k < K && S.w[l * K + k] != 0.0f) {
                 const int e = l * K + k;
                 const int iy = y + S.tap_dy[e], ix = x + S.tap_dx[e];
                 if (iy >= 0 && iy < A.H && ix >= 0 && ix < A.W)
@@ -281,7 +282,7 @@ conv_soft_bwd_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict
                         if (iy >= 0 && iy < A.H && ix >= 0 && ix < A.W) {
                             const int64_t idx = (((int64_t)S.tap_c[e] * A.H + iy) * A.W + ix) * A.ldb + b;
                             acc_w[l * KT + k] += gl * __ldg(&A.x[idx]);
-                            if (gx) atomicAdd(&gx[idx], gl * S.w[e]);
+                            if (gx && S.w[e] != 0.0f) atomicAdd(&gx[idx], gl * S.w[e]);
                         }
                     }
                 }

@@ -83,7 +83,7 @@ fc_soft_fwd_kernel(const float4* __restrict__ x, int64_t nv, const int32_t* __re
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
             for (int k = 0; k < KT; ++k) {
-                if (k < K) {
+                if (k < K && wr[j * KT + k] != 0.0f) {     // skip one-hot zeros
                     const float wk = wr[j * KT + k];
                     const float4 xv = __ldg(rows[j * KT + k] + v);
                     acc.x += wk * xv.x; acc.y += wk * xv.y; acc.z += wk * xv.z; acc.w += wk * xv.w;
@@ -164,7 +164,7 @@ fc_soft_bwd_kernel(const float4* __restrict__ x, int64_t nv, const int32_t* __re
                 const int64_t row = S.cand[j * K + k];
                 const float4 xv = __ldg(&x[row * nv + v]);
                 acc_w[j * KT + k] += ga[0][j] * xv.x + ga[1][j] * xv.y + ga[2][j] * xv.z + ga[3][j] * xv.w;
-                if (gx) {
+                if (gx && S.w[j * K + k] != 0.0f) {
                     const float wk = S.w[j * K + k];
                     atomicAdd(&gx[row * nv + v],
                               make_float4(ga[0][j] * wk, ga[1][j] * wk, ga[2][j] * wk, ga[3][j] * wk));

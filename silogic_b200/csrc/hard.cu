@@ -10,6 +10,12 @@
 namespace slg {
 
 constexpr int HB_THREADS = 256;
+#ifndef SLG_CONV_VPT
+#define SLG_CONV_VPT 1          // 128-sample vectors per thread in the conv tree kernel
+#endif
+#ifndef SLG_CONV_MINB
+#define SLG_CONV_MINB 4         // minimum resident CTAs per SM requested from the compiler
+#endif
 
 // lanes per node along the word axis: power of two, <= 32, >= nvec when small
 static inline int pick_vt(int64_t nvec) {
@@ -61,32 +67,44 @@ struct Tree {
     static constexpr int NODES = (LEAVES - 1) / (AR - 1);
 };
 
-template <int AR, int DEPTH>
-__global__ void __launch_bounds__(HB_THREADS)
+// receptive-field tap r = c*k*k + dy*k + dx -> (c, dy, dx); constant divisors for 3x3
+__device__ __forceinline__ void decode_tap(int r, int k, int& c, int& dy, int& dx) {
+    if (k == 3) { c = r / 9; const int q = r - c * 9; dy = q / 3; dx = q - dy * 3; }
+    else { const int kk = k * k; c = r / kk; const int q = r - c * kk; dy = q / k; dx = q - dy * k; }
+}
+
+// One thread: output channel n, one pooled position, VPT vectors of 128 samples.
+// Tap addresses of each pre-pool position are computed once and shared by the
+// thread's vectors.
+template <int AR, int DEPTH, int POOL>
+__global__ void __launch_bounds__(HB_THREADS, SLG_CONV_MINB)
 conv_hard_kernel(const uint4* __restrict__ x, int64_t cin, int H, int W, int64_t nvec,
                  const int32_t* __restrict__ leaf, const uint64_t* __restrict__ tt, int kernel,
-                 int pad, int64_t n_out, int64_t wire_r, int pool, int Hp, int Wp,
+                 int pad, int64_t n_out, int64_t wire_r, int Hp, int Wp,
                  uint4* __restrict__ out, int vt_shift) {
     constexpr int LEAVES = Tree<AR, DEPTH>::LEAVES;
     constexpr int NODES = Tree<AR, DEPTH>::NODES;
+    constexpr int VPT = SLG_CONV_VPT;
     const int vt = 1 << vt_shift;
-    const int ppb = HB_THREADS >> vt_shift;  // positions per block
-    const int64_t npos = (int64_t)Hp * Wp;
-    const int64_t tiles = (npos + ppb - 1) / ppb;
+    const int ppb = HB_THREADS >> vt_shift;         // positions per block
+    const int npos = Hp * Wp;
+    const int tiles = (npos + ppb - 1) / ppb;
     const int64_t n = blockIdx.x / tiles;
-    const int64_t pos = (blockIdx.x % tiles) * ppb + (threadIdx.x >> vt_shift);
-    const int64_t v = (int64_t)blockIdx.y * vt + (threadIdx.x & (vt - 1));
-    if (n >= n_out || pos >= npos || v >= nvec) return;
-    const int py = (int)(pos / Wp), px = (int)(pos % Wp);
-    const int kk = kernel * kernel;
+    const int pos = (blockIdx.x % tiles) * ppb + (threadIdx.x >> vt_shift);
+    const int64_t v0 = (int64_t)blockIdx.y * vt * VPT + (threadIdx.x & (vt - 1));
+    if (n >= n_out || pos >= npos || v0 >= nvec) return;
+    const int py = pos / Wp, px = pos - py * Wp;
+    const int64_t plane = (int64_t)H * W * nvec;
 
-    int lc[LEAVES], ly[LEAVES], lx[LEAVES];
+    const uint4* lp[LEAVES];                        // channel plane of each leaf (+ this lane's v)
+    int ly[LEAVES], lx[LEAVES];
 #pragma unroll
     for (int l = 0; l < LEAVES; ++l) {
-        int r = __ldg(&leaf[n * LEAVES + l]);
-        lc[l] = r / kk;
-        ly[l] = (r % kk) / kernel - pad;
-        lx[l] = r % kernel - pad;
+        int c, dy, dx;
+        decode_tap(__ldg(&leaf[n * LEAVES + l]), kernel, c, dy, dx);
+        lp[l] = x + c * plane + v0;
+        ly[l] = dy - pad;
+        lx[l] = dx - pad;
     }
     constexpr bool PRE = NODES * (1 << AR) <= 64;   // leaf masks of every node fit in registers
     uint64_t tn[NODES];
@@ -96,25 +114,46 @@ conv_hard_kernel(const uint4* __restrict__ x, int64_t cin, int H, int W, int64_t
         tn[i] = __ldg(&tt[n * NODES + i]);
         if constexpr (PRE) lut_masks<AR>(tn[i], mk[i]);
     }
-
-    uint4 acc = make_uint4(0, 0, 0, 0);
-    for (int oy = 0; oy < pool; ++oy) {
-        for (int ox = 0; ox < pool; ++ox) {
-            const int y = py * pool + oy, xx = px * pool + ox;
-            uint4 res;
-            if (n < wire_r) {
-                res = __ldg(&x[((n * H + y) * (int64_t)W + xx) * nvec + v]);
-            } else {
+    const bool wired = n < wire_r;
+    int nu = 0;                                     // vectors this thread owns (<= VPT)
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) nu += (v0 + (int64_t)u * vt < nvec) ? 1 : 0;
+    uint4 acc[VPT];
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) acc[u] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int oy = 0; oy < POOL; ++oy) {
+#pragma unroll
+        for (int ox = 0; ox < POOL; ++ox) {
+            const int y = py * POOL + oy, xx = px * POOL + ox;
+            if (wired) {
+                const uint4* src = x + n * plane + (int64_t)(y * W + xx) * nvec + v0;
+#pragma unroll
+                for (int u = 0; u < VPT; ++u)
+                    if (u < nu) {
+                        const uint4 t = __ldg(src + (int64_t)u * vt);
+                        acc[u].x |= t.x; acc[u].y |= t.y; acc[u].z |= t.z; acc[u].w |= t.w;
+                    }
+                continue;
+            }
+            const uint4* tp[LEAVES];
+            bool ok[LEAVES];
+#pragma unroll
+            for (int l = 0; l < LEAVES; ++l) {
+                const int iy = y + ly[l], ix = xx + lx[l];
+                ok[l] = (unsigned)iy < (unsigned)H && (unsigned)ix < (unsigned)W;
+                tp[l] = lp[l] + (ok[l] ? (int64_t)(iy * W + ix) * nvec : 0);
+            }
+#pragma unroll
+            for (int u = 0; u < VPT; ++u) {
+                if (u >= nu) break;
                 uint32_t val[LEAVES][4];
 #pragma unroll
                 for (int l = 0; l < LEAVES; ++l) {
-                    const int iy = y + ly[l], ix = xx + lx[l];
-                    uint4 u = make_uint4(0, 0, 0, 0);
-                    if (iy >= 0 && iy < H && ix >= 0 && ix < W)
-                        u = __ldg(&x[((lc[l] * (int64_t)H + iy) * W + ix) * nvec + v]);
-                    val[l][0] = u.x; val[l][1] = u.y; val[l][2] = u.z; val[l][3] = u.w;
+                    uint4 t = make_uint4(0, 0, 0, 0);
+                    if (ok[l]) t = __ldg(tp[l] + (int64_t)u * vt);
+                    val[l][0] = t.x; val[l][1] = t.y; val[l][2] = t.z; val[l][3] = t.w;
                 }
-                // bottom-up: level i has LEAVES / AR^(i+1) nodes
                 int width = LEAVES, node_base = 0;
 #pragma unroll
                 for (int lev = 0; lev < DEPTH; ++lev) {
@@ -133,12 +172,13 @@ conv_hard_kernel(const uint4* __restrict__ x, int64_t cin, int H, int W, int64_t
                     node_base += nn;
                     width = nn;
                 }
-                res = make_uint4(val[0][0], val[0][1], val[0][2], val[0][3]);
+                acc[u].x |= val[0][0]; acc[u].y |= val[0][1]; acc[u].z |= val[0][2]; acc[u].w |= val[0][3];
             }
-            acc.x |= res.x; acc.y |= res.y; acc.z |= res.z; acc.w |= res.w;
         }
     }
-    out[(n * npos + pos) * nvec + v] = acc;
+#pragma unroll
+    for (int u = 0; u < VPT; ++u)
+        if (u < nu) out[(n * npos + pos) * nvec + v0 + (int64_t)u * vt] = acc[u];
 }
 
 // --------------------------------------------------------------- GroupSum
@@ -235,8 +275,12 @@ template <int AR, int D>
 static void launch_conv(dim3 g, cudaStream_t st, const uint4* x, int64_t cin, int H, int W,
                         int64_t nvec, const int32_t* leaf, const uint64_t* tt, int kernel, int pad,
                         int64_t n_out, int64_t wire_r, int pool, int Hp, int Wp, uint4* out, int vs) {
-    conv_hard_kernel<AR, D><<<g, HB_THREADS, 0, st>>>(x, cin, H, W, nvec, leaf, tt, kernel, pad, n_out,
-                                                      wire_r, pool, Hp, Wp, out, vs);
+    if (pool == 2)
+        conv_hard_kernel<AR, D, 2><<<g, HB_THREADS, 0, st>>>(x, cin, H, W, nvec, leaf, tt, kernel, pad,
+                                                             n_out, wire_r, Hp, Wp, out, vs);
+    else
+        conv_hard_kernel<AR, D, 1><<<g, HB_THREADS, 0, st>>>(x, cin, H, W, nvec, leaf, tt, kernel, pad,
+                                                             n_out, wire_r, Hp, Wp, out, vs);
 }
 
 extern "C" int slg_conv_hard(const uint64_t* x, int64_t cin, int64_t H, int64_t W, int64_t ldw,
@@ -256,13 +300,14 @@ extern "C" int slg_conv_hard(const uint64_t* x, int64_t cin, int64_t H, int64_t 
     if (n_out == 0 || Hp == 0 || Wp == 0) return SLG_OK;
     if (!leaf || !tt) return set_error(SLG_ERR_ARG, "slg_conv_hard: null pointer");
     const int64_t nvec = ldw / 2;
-    const int vt = pick_vt(nvec);
+    const int vt = pick_vt(cdiv(nvec, SLG_CONV_VPT));
     int vs = 0;
     while ((1 << vs) < vt) ++vs;
     const int64_t ppb = HB_THREADS / vt;
     const int64_t tiles = cdiv(Hp * Wp, ppb);
-    const int64_t gy = cdiv(nvec, vt);
-    if (gy > 65535 || n_out * tiles > 0x7fffffffLL) return set_error(SLG_ERR_ARG, "slg_conv_hard: grid too large");
+    const int64_t gy = cdiv(nvec, vt * SLG_CONV_VPT);
+    if (gy > 65535 || n_out * tiles > 0x7fffffffLL || H * W > (1 << 24))
+        return set_error(SLG_ERR_ARG, "slg_conv_hard: grid too large");
     dim3 grid((unsigned)(n_out * tiles), (unsigned)gy);
     auto xs = reinterpret_cast<const uint4*>(x);
     auto os = reinterpret_cast<uint4*>(out);

@@ -104,47 +104,94 @@ __global__ void unpack_kernel(const uint64_t* __restrict__ p, int64_t F, int64_t
     out[i] = (uint8_t)((p[f * ldw + (b >> 6)] >> (b & 63)) & 1ull);
 }
 
+// 32x32 bit transpose across a warp: on entry lane l holds row l (bit t = M[l][t]);
+// on exit lane t holds column t (bit l = M[l][t]).  Five block-swap stages.
+__device__ __forceinline__ uint32_t warp_transpose32(uint32_t x, int lane) {
+    const uint32_t masks[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+    for (int s = 0; s < 5; ++s) {
+        const int j = 16 >> s;
+        const uint32_t m = masks[s];
+        const uint32_t other = __shfl_xor_sync(0xffffffffu, x, j);
+        x = (lane & j) ? ((x & ~m) | ((other & ~m) >> j)) : ((x & m) | ((other & m) << j));
+    }
+    return x;
+}
+
 // Thermometer: x [B, C, HW] -> out [C*T, HW, ldw]
-// tile: 64 samples x PK_FT pixel-features (feature f = c*HW + p)
+// tile: 64 samples x PK_FT pixel-features (feature f = c*HW + p), float4 loads when
+// rows allow.  For one feature, lane l builds the thermometer code of samples l and
+// 32+l (bit t = 1[x passes threshold t]) -- by binary search when the shared
+// thresholds are sorted -- and a warp bit-transpose hands lane t the 64-sample word
+// of threshold t, so T words cost ~2 transposes instead of 2T ballots.
 __global__ void __launch_bounds__(PK_THREADS)
 thermo_kernel(const float* __restrict__ x, int64_t B, int64_t C, int64_t HW,
-              const float* __restrict__ thr, int T, int mode, uint64_t* __restrict__ out, int64_t ldw) {
+              const float* __restrict__ thr, int T, int mode, int sorted,
+              uint64_t* __restrict__ out, int64_t ldw) {
     __shared__ float tile[64][PK_FT + 1];
+    __shared__ float sthr[32];
     const int64_t F = C * HW;
     const int64_t w = blockIdx.y;
     const int64_t f0 = (int64_t)blockIdx.x * PK_FT;
     const int64_t b0 = w * 64;
-    for (int i = threadIdx.x; i < 64 * PK_FT; i += PK_THREADS) {
-        int s = i / PK_FT, f = i % PK_FT;
-        int64_t b = b0 + s, ff = f0 + f;
-        tile[s][f] = (b < B && ff < F) ? x[b * F + ff] : 0.0f;
+    const bool vec = (F % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+    if (vec) {
+        for (int i = threadIdx.x; i < 64 * (PK_FT / 4); i += PK_THREADS) {
+            const int s = i / (PK_FT / 4), q = (i % (PK_FT / 4)) * 4;
+            const int64_t b = b0 + s, ff = f0 + q;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (b < B && ff + 4 <= F) v = __ldg(reinterpret_cast<const float4*>(x + b * F + ff));
+            else if (b < B)
+                for (int e = 0; e < 4; ++e) if (ff + e < F) (&v.x)[e] = x[b * F + ff + e];
+            tile[s][q] = v.x; tile[s][q + 1] = v.y; tile[s][q + 2] = v.z; tile[s][q + 3] = v.w;
+        }
+    } else {
+        for (int i = threadIdx.x; i < 64 * PK_FT; i += PK_THREADS) {
+            const int s = i / PK_FT, f = i % PK_FT;
+            const int64_t b = b0 + s, ff = f0 + f;
+            tile[s][f] = (b < B && ff < F) ? x[b * F + ff] : 0.0f;
+        }
     }
-    __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t lo_ok = __ballot_sync(0xffffffffu, b0 + lane < B);
     const uint32_t hi_ok = __ballot_sync(0xffffffffu, b0 + 32 + lane < B);
     const int per = PK_FT / (PK_THREADS / 32);
-    for (int j = 0; j < per; ++j) {
-        int f = warp * per + j;
-        int64_t ff = f0 + f;
-        if (ff >= F) break;  // warp-uniform
-        int64_t c = ff / HW, p = ff % HW;
-        float v0 = tile[lane][f], v1 = tile[32 + lane][f];
-        for (int t = 0; t < T; ++t) {
-            bool b_lo, b_hi;
-            int64_t ch;
-            if (mode == 0) {
-                float th = thr[t];
-                b_lo = v0 >= th; b_hi = v1 >= th;
-                ch = (int64_t)t * C + c;
+    for (int t0 = 0; t0 < T; t0 += 32) {
+        const int nt = min(32, T - t0);
+        __syncthreads();
+        if (mode == 0 && threadIdx.x < nt) sthr[threadIdx.x] = thr[t0 + threadIdx.x];
+        __syncthreads();
+        for (int j = 0; j < per; ++j) {
+            const int f = warp * per + j;
+            const int64_t ff = f0 + f;
+            if (ff >= F) break;  // warp-uniform
+            const int64_t c = ff / HW, p = ff % HW;
+            const float v0 = tile[lane][f], v1 = tile[32 + lane][f];
+            uint32_t m0 = 0, m1 = 0;
+            if (mode == 0 && sorted) {
+                int lo0 = 0, hi0 = nt, lo1 = 0, hi1 = nt;      // count of thresholds <= v
+#pragma unroll
+                for (int it = 0; it < 6; ++it) {
+                    if (lo0 < hi0) { const int md = (lo0 + hi0) >> 1; if (v0 >= sthr[md]) lo0 = md + 1; else hi0 = md; }
+                    if (lo1 < hi1) { const int md = (lo1 + hi1) >> 1; if (v1 >= sthr[md]) lo1 = md + 1; else hi1 = md; }
+                }
+                m0 = lo0 >= 32 ? 0xffffffffu : ((1u << lo0) - 1u);
+                m1 = lo1 >= 32 ? 0xffffffffu : ((1u << lo1) - 1u);
             } else {
-                float th = thr[ff * T + t];
-                b_lo = (v0 - th) > 0.0f; b_hi = (v1 - th) > 0.0f;
-                ch = c * T + t;
+                for (int t = 0; t < nt; ++t) {
+                    const float th = mode == 0 ? sthr[t] : thr[ff * T + t0 + t];
+                    const bool a0 = mode == 0 ? (v0 >= th) : ((v0 - th) > 0.0f);
+                    const bool a1 = mode == 0 ? (v1 >= th) : ((v1 - th) > 0.0f);
+                    m0 |= (uint32_t)a0 << t;
+                    m1 |= (uint32_t)a1 << t;
+                }
             }
-            uint32_t lo = __ballot_sync(0xffffffffu, b_lo) & lo_ok;
-            uint32_t hi = __ballot_sync(0xffffffffu, b_hi) & hi_ok;
-            if (lane == 0) out[(ch * HW + p) * ldw + w] = ((uint64_t)hi << 32) | lo;
+            const uint32_t lo = warp_transpose32(m0, lane) & lo_ok;
+            const uint32_t hi = warp_transpose32(m1, lane) & hi_ok;
+            if (lane < nt) {
+                const int64_t ch = mode == 0 ? (int64_t)(t0 + lane) * C + c : c * T + t0 + lane;
+                out[(ch * HW + p) * ldw + w] = ((uint64_t)hi << 32) | lo;
+            }
         }
     }
 }
@@ -197,7 +244,7 @@ extern "C" int slg_unpack_u8(const uint64_t* p, int64_t F, int64_t ldw, int64_t 
 
 extern "C" int slg_thermo_pack(const float* x, int64_t B, int64_t C, int64_t HW, const float* thr,
                                int64_t T, int32_t mode, uint64_t* out, int64_t ldw, void* stream) {
-    if (B < 0 || C <= 0 || HW <= 0 || T <= 0 || (mode != 0 && mode != 1))
+    if (B < 0 || C <= 0 || HW <= 0 || T <= 0 || mode < 0 || mode > 2)
         return set_error(SLG_ERR_ARG, "slg_thermo_pack: bad arguments");
     if (B == 0) return SLG_OK;
     int64_t nw = cdiv(B, 64);
@@ -205,7 +252,10 @@ extern "C" int slg_thermo_pack(const float* x, int64_t B, int64_t C, int64_t HW,
     if (nw > 65535) return set_error(SLG_ERR_ARG, "slg_thermo_pack: batch too large");
     if (!x || !thr || !out) return set_error(SLG_ERR_ARG, "slg_thermo_pack: null pointer");
     dim3 grid((unsigned)cdiv(C * HW, PK_FT), (unsigned)nw);
-    thermo_kernel<<<grid, PK_THREADS, 0, as_stream(stream)>>>(x, B, C, HW, thr, (int)T, mode, out, ldw);
+    // mode 2 = mode 0 with thresholds the caller guarantees sorted ascending
+    const int sorted = mode == 2 ? 1 : 0;
+    thermo_kernel<<<grid, PK_THREADS, 0, as_stream(stream)>>>(x, B, C, HW, thr, (int)T, mode == 2 ? 0 : mode,
+                                                             sorted, out, ldw);
     if (ldw > nw) {
         int64_t rows = C * T * HW, n = rows * (ldw - nw);
         zero_tail_kernel<<<(unsigned)cdiv(n, 256), 256, 0, as_stream(stream)>>>(out, rows, ldw, nw);

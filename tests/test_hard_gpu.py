@@ -190,3 +190,18 @@ def test_forward_images_fuses_thermometer_vs_oracle():
     bp = convert_logic_conv_net(m.cuda())
     got = bp.forward_images(img.cuda(), th) * 4.0
     np.testing.assert_array_equal(np.rint(got.cpu().numpy()), ref)
+
+
+@pytest.mark.parametrize("th", [[0.5], [1 / 6, 2 / 6, 3 / 6, 4 / 6, 5 / 6],
+                                [(i + 1) / 32 for i in range(31)], [0.7, 0.2, 0.5],
+                                [(i + 1) / 40 for i in range(39)], [0.3, 0.3, 0.6]])
+def test_thermometer_pack_sorted_unsorted_and_long_vs_oracle(th):
+    from silogic_b200 import _hard
+    img = torch.rand(70, 3, 5, 7, generator=torch.Generator().manual_seed(len(th)))
+    img[0, 0, 0, :len(th[:7])] = torch.tensor(th[:7])                  # exact threshold values
+    h = _hard.thermo_pack(img.cuda(), th)
+    got = _hard.unpack(h.view(-1, h.shape[-1]), 70).view(70, -1).cpu().numpy()
+    ref = OH.thermometer_bits(img.numpy(), th).reshape(70, -1)
+    np.testing.assert_array_equal(got, ref)
+    h2 = _hard.thermo_pack(img.cuda(), torch.tensor(th).cuda())      # tensor thresholds path
+    np.testing.assert_array_equal(h2.cpu().numpy(), h.cpu().numpy())
