@@ -355,8 +355,8 @@ def run_soft(cfg, B, steps, warmup, rank, ws, dev):
         logits = model(xi)
         (logits * rmat).sum().backward()
         if ws > 1:      # data parallel: one all-reduce of every parameter gradient
-            bucket = torch.cat([p.grad.reshape(-1) for p in params])
-            torch.distributed.all_reduce(bucket)
+            from silogic_b200.distributed import allreduce_gradients
+            allreduce_gradients(params)
         return logits
 
     for _ in range(warmup):
