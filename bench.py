@@ -425,6 +425,7 @@ def main():
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--cpu-sample", type=int, default=None)
     ap.add_argument("--no-soft", action="store_true")
+    ap.add_argument("--soft-only", action="store_true", help="profile the soft leg alone")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the hard batch (small cases for profiling)")
     a = ap.parse_args()
@@ -458,10 +459,19 @@ def main():
         return
 
     if ws > 1:
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"      # keep stdout to the one JSON line
         torch.distributed.init_process_group("nccl")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     B = cfg["hard_batch"] // (ws if cfg["scaling"] == "strong" else 1)
+    if a.soft_only:
+        soft = run_soft(cfg, cfg["soft_batch"], a.steps, warmup, rank, ws, dev)
+        if rank == 0:
+            print(json.dumps({"metric": "soft fwd+bwd samples/s", "config": cfg["name"],
+                              "value": cfg["soft_batch"] * ws / (soft["ms"] * 1e-3),
+                              "ms_per_step": soft["ms"]}))
+        return
     r = run_hard(cfg, B, a.steps, warmup, rank, ws, dev)
     soft = None
     if not a.no_soft and cfg["soft_batch"]:

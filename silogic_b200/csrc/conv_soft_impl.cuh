@@ -99,13 +99,30 @@ __device__ __forceinline__ void conv_stage(ConvSmem<NODE, AR, D>& S, const ConvA
     __syncthreads();
 }
 
+// Tap positions of one warp's pool window: pos[q*L*KT + l*K + k] = c*H*W + iy*W + ix of
+// candidate k of leaf l at window element q, or -1 outside the image.  Warp-uniform,
+// so it is computed once per warp and reused for every sample of the chunk.
+template <int NODE, int AR, int D, int KT>
+__device__ __forceinline__ void conv_fill_pos(const ConvSmem<NODE, AR, D>& S, const ConvArgs& A, int py,
+                                              int px, int* pos, int lane) {
+    constexpr int L = TreeShape<AR, D>::L;
+    const int K = A.K, HW = A.H * A.W;
+    for (int i = lane; i < A.pool * A.pool * L * K; i += 32) {
+        const int q = i / (L * K), e = i % (L * K);
+        const int y = py * A.pool + q / A.pool, x = px * A.pool + q % A.pool;
+        const int iy = y + S.tap_dy[e], ix = x + S.tap_dx[e];
+        pos[q * L * KT + e] = (iy >= 0 && iy < A.H && ix >= 0 && ix < A.W) ? S.tap_c[e] * HW + iy * A.W + ix : -1;
+    }
+    __syncwarp();
+}
+
 template <int NODE, int AR, int D, int KT>
 __device__ __forceinline__ float conv_tree_value(const ConvSmem<NODE, AR, D>& S, const ConvArgs& A,
-                                                 int y, int x, int64_t b, float (&vals)[2 * TreeShape<AR, D>::L]) {
+                                                 const int* __restrict__ posq, int64_t b,
+                                                 float (&vals)[2 * TreeShape<AR, D>::L]) {
     constexpr int L = TreeShape<AR, D>::L;
     constexpr int NPS = NodeStage<NODE, AR>::NPS;
     const int K = A.K;
-    // leaves into vals[0..L)
 #pragma unroll
     for (int l = 0; l < L; ++l) {
         float s = 0.f;
@@ -113,15 +130,12 @@ __device__ __forceinline__ float conv_tree_value(const ConvSmem<NODE, AR, D>& S,
         for (int k = 0; k < KT; ++k) {
             // zero weights (one-hot straight-through selection) contribute nothing: skip the load
             if (k < K && S.w[l * K + k] != 0.0f) {
-                const int e = l * K + k;
-                const int iy = y + S.tap_dy[e], ix = x + S.tap_dx[e];
-                if (iy >= 0 && iy < A.H && ix >= 0 && ix < A.W)
-                    s += S.w[e] * __ldg(&A.x[(((int64_t)S.tap_c[e] * A.H + iy) * A.W + ix) * A.ldb + b]);
+                const int p = posq[l * K + k];
+                if (p >= 0) s += S.w[l * K + k] * __ldg(&A.x[(int64_t)p * A.ldb + b]);
             }
         }
         vals[l] = s;
     }
-    // levels: level i nodes stored after the previous level's values
     int in_base = 0, out_base = L, width = L, node_base = 0;
 #pragma unroll
     for (int lev = 0; lev < D; ++lev) {
@@ -151,23 +165,25 @@ conv_soft_fwd_kernel(ConvArgs A, float* __restrict__ y) {
     const int64_t n = blockIdx.x / tiles;
     const int p = (blockIdx.x % tiles) * CS_WARPS + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    __shared__ int s_pos[CS_WARPS][4 * L * KT];
     const bool wired = n < A.wire_r;
     if (!wired) conv_stage<NODE, AR, D>(S, A, n);
     if (p >= npos) return;
     const int py = p / A.Wp, px = p % A.Wp;
+    int* pos = s_pos[threadIdx.x >> 5];
+    if (!wired) conv_fill_pos<NODE, AR, D, KT>(S, A, py, px, pos, lane);
     const int64_t b0 = (int64_t)blockIdx.y * (32 * CS_ITER);
     float vals[2 * L];
     for (int it = 0; it < CS_ITER; ++it) {
         const int64_t b = b0 + it * 32 + lane;
         if (b >= A.ldb) break;
         float best = 0.f;
-        for (int oy = 0; oy < A.pool; ++oy)
-            for (int ox = 0; ox < A.pool; ++ox) {
-                const int yy = py * A.pool + oy, xx = px * A.pool + ox;
-                const float v = wired ? __ldg(&A.x[((n * A.H + yy) * (int64_t)A.W + xx) * A.ldb + b])
-                                      : conv_tree_value<NODE, AR, D, KT>(S, A, yy, xx, b, vals);
-                if ((oy | ox) == 0 || v > best) best = v;
-            }
+        for (int q = 0; q < A.pool * A.pool; ++q) {
+            const int yy = py * A.pool + q / A.pool, xx = px * A.pool + q % A.pool;
+            const float v = wired ? __ldg(&A.x[((n * A.H + yy) * (int64_t)A.W + xx) * A.ldb + b])
+                                  : conv_tree_value<NODE, AR, D, KT>(S, A, pos + q * L * KT, b, vals);
+            if (q == 0 || v > best) best = v;
+        }
         y[((n * npos) + p) * A.ldb + b] = best;
     }
 }
@@ -213,6 +229,9 @@ conv_soft_bwd_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict
         return;
     }
     conv_stage<NODE, AR, D>(S, A, n);
+    __shared__ int s_pos[CS_WARPS][4 * L * KT];
+    int* pos = s_pos[warp];
+    if (p < npos) conv_fill_pos<NODE, AR, D, KT>(S, A, p / A.Wp, p % A.Wp, pos, lane);
     float acc_w[L * KT];
 #pragma unroll
     for (int e = 0; e < L * KT; ++e) acc_w[e] = 0.f;
@@ -231,17 +250,16 @@ conv_soft_bwd_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict
             if (b >= A.ldb) break;
             const float g = gy[((n * npos) + p) * A.ldb + b];
             // argmax position of the pool window (first maximum)
-            int by = py * A.pool, bx = px * A.pool;
+            int bq = 0;
             if (A.pool > 1) {
                 float best = 0.f;
-                for (int oy = 0; oy < A.pool; ++oy)
-                    for (int ox = 0; ox < A.pool; ++ox) {
-                        const int yy = py * A.pool + oy, xx = px * A.pool + ox;
-                        const float v = conv_tree_value<NODE, AR, D, KT>(S, A, yy, xx, b, vals);
-                        if ((oy | ox) == 0 || v > best) { best = v; by = yy; bx = xx; }
-                    }
+                for (int q = 0; q < A.pool * A.pool; ++q) {
+                    const float v = conv_tree_value<NODE, AR, D, KT>(S, A, pos + q * L * KT, b, vals);
+                    if (q == 0 || v > best) { best = v; bq = q; }
+                }
             }
-            conv_tree_value<NODE, AR, D, KT>(S, A, by, bx, b, vals);
+            const int* posq = pos + bq * L * KT;
+            conv_tree_value<NODE, AR, D, KT>(S, A, posq, b, vals);
             // reverse pass through the tree: adjoints indexed like vals; level bases:
             // leaves at 0, level i (1..D) at L + sum_{j<i} L/AR^j
             float adj[2 * L];
@@ -278,9 +296,8 @@ conv_soft_bwd_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict
                 for (int k = 0; k < KT; ++k) {
                     if (k < K) {
                         const int e = l * K + k;
-                        const int iy = by + S.tap_dy[e], ix = bx + S.tap_dx[e];
-                        if (iy >= 0 && iy < A.H && ix >= 0 && ix < A.W) {
-                            const int64_t idx = (((int64_t)S.tap_c[e] * A.H + iy) * A.W + ix) * A.ldb + b;
+                        if (posq[e] >= 0) {
+                            const int64_t idx = (int64_t)posq[e] * A.ldb + b;
                             acc_w[l * KT + k] += gl * __ldg(&A.x[idx]);
                             if (gx && S.w[e] != 0.0f) atomicAdd(&gx[idx], gl * S.w[e]);
                         }
