@@ -25,38 +25,59 @@ static inline int pick_vt(int64_t nvec) {
 }
 
 // ----------------------------------------------------------------- FC layer
+#ifndef SLG_FC_VPT
+#define SLG_FC_VPT 4            // 128-sample vectors per thread in the FC kernel
+#endif
+#ifndef SLG_FC_MINB
+#define SLG_FC_MINB 1
+#endif
+
+// One thread: node o, SLG_FC_VPT vectors of 128 samples (stride vt), so the node's
+// wiring, truth table and masks are loaded once and several data loads are in flight.
 template <int AR>
-__global__ void __launch_bounds__(HB_THREADS)
+__global__ void __launch_bounds__(HB_THREADS, SLG_FC_MINB)
 fc_hard_kernel(const uint4* __restrict__ x, int64_t nvec, const int32_t* __restrict__ idx,
                const uint64_t* __restrict__ tt, int64_t out_dim, int64_t wire_r,
                uint4* __restrict__ out, int vt_shift) {
+    constexpr int VPT = SLG_FC_VPT;
     const int vt = 1 << vt_shift;
     const int64_t o = (int64_t)blockIdx.x * (HB_THREADS >> vt_shift) + (threadIdx.x >> vt_shift);
-    const int64_t v = (int64_t)blockIdx.y * vt + (threadIdx.x & (vt - 1));
-    if (o >= out_dim || v >= nvec) return;
-    uint4 r;
+    const int64_t v0 = (int64_t)blockIdx.y * vt * VPT + (threadIdx.x & (vt - 1));
+    if (o >= out_dim || v0 >= nvec) return;
     if (o < wire_r) {
-        r = __ldg(&x[o * nvec + v]);
-    } else {
-        uint4 in[AR];
 #pragma unroll
-        for (int j = 0; j < AR; ++j) {
-            const int64_t row = __ldg(&idx[o * AR + j]);
-            in[j] = __ldg(&x[row * nvec + v]);
+        for (int u = 0; u < VPT; ++u) {
+            const int64_t v = v0 + (int64_t)u * vt;
+            if (v < nvec) out[o * nvec + v] = __ldg(&x[o * nvec + v]);
         }
-        uint32_t m[1 << AR];
-        lut_masks<AR>(__ldg(&tt[o]), m);
+        return;
+    }
+    const uint4* rows[AR];
+#pragma unroll
+    for (int j = 0; j < AR; ++j) rows[j] = x + (int64_t)__ldg(&idx[o * AR + j]) * nvec;
+    uint4 in[VPT][AR];
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) {
+        const int64_t v = v0 + (int64_t)u * vt;
+#pragma unroll
+        for (int j = 0; j < AR; ++j) in[u][j] = v < nvec ? __ldg(rows[j] + v) : make_uint4(0, 0, 0, 0);
+    }
+    uint32_t m[1 << AR];
+    lut_masks<AR>(__ldg(&tt[o]), m);
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) {
+        const int64_t v = v0 + (int64_t)u * vt;
+        if (v >= nvec) break;
         uint32_t res[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             uint32_t vv[AR];
 #pragma unroll
-            for (int j = 0; j < AR; ++j) vv[j] = u4get(in[j], c);
+            for (int j = 0; j < AR; ++j) vv[j] = u4get(in[u][j], c);
             res[c] = lut_eval_m<AR>(vv, m);
         }
-        r = make_uint4(res[0], res[1], res[2], res[3]);
+        out[o * nvec + v] = make_uint4(res[0], res[1], res[2], res[3]);
     }
-    out[o * nvec + v] = r;
 }
 
 // ------------------------------------------------------------- conv tree
@@ -249,11 +270,11 @@ extern "C" int slg_fc_hard(const uint64_t* x, int64_t in_dim, int64_t ldw, const
     if (out_dim == 0) return SLG_OK;
     if (!idx || !tt) return set_error(SLG_ERR_ARG, "slg_fc_hard: null pointer");
     const int64_t nvec = ldw / 2;
-    const int vt = pick_vt(nvec);
+    const int vt = pick_vt(cdiv(nvec, SLG_FC_VPT));
     int vs = 0;
     while ((1 << vs) < vt) ++vs;
     const int64_t npb = HB_THREADS / vt;
-    const int64_t gy = cdiv(nvec, vt);
+    const int64_t gy = cdiv(nvec, vt * SLG_FC_VPT);
     if (gy > 65535) return set_error(SLG_ERR_ARG, "slg_fc_hard: batch too large");
     dim3 grid((unsigned)cdiv(out_dim, npb), (unsigned)gy);
     auto xs = reinterpret_cast<const uint4*>(x);
