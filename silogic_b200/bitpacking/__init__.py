@@ -7,6 +7,7 @@ import numpy as np
 import torch
 
 from .. import _hard
+from .plan import HardPlan, HardGraph
 from .convert import convert_logic_net, convert_logic_conv_net, convert_layer, convert_head
 from .packed import (BitpackedNet, BitpackedConvNet, BitpackedConvGPUNet, BitpackedGPULayer,
                      BitpackedConvGPULayer, packed_unfold_gpu, packed_or_pool_gpu)

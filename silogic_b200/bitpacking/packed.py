@@ -9,6 +9,7 @@ import torch
 
 from .. import _hard
 from ..functional import gate16_lut_codes
+from .plan import HardGraph
 
 
 def _dev(device=None):
@@ -19,6 +20,12 @@ def _as_cuda(x, device=None):
     if isinstance(x, np.ndarray):
         return torch.from_numpy(np.ascontiguousarray(x)).to(_dev(device), non_blocking=True)
     return x
+
+
+def _plan_device(plan):
+    for st in plan.steps:
+        return st["tt"].device
+    return _dev()
 
 
 def _packed_in(x, device=None):
@@ -115,17 +122,58 @@ class BitpackedNet:
     """End-to-end bit-packed ``LogicNet`` on the GPU.  ``net(x)`` with ``x`` ``[B, in]``
     uint8 -> ``[B, num_classes]`` float32 = counts / tau (``packed_model.py:75-102``)."""
 
-    def __init__(self, plan, head):
+    #: batch shapes whose CUDA graphs are kept (each holds its activations' memory)
+    max_graphs = 4
+
+    def __init__(self, plan, head, graphs=True):
         self.plan, self.head = plan, head
         self.num_layers = len(plan.steps)
+        self.graphs = graphs
+        self._graphs = {}
+        self.device = _plan_device(plan)
+
+    def _graph_for(self, x, thresholds=None, mode=0):
+        """Cached :class:`HardGraph` for this input shape/dtype (and thresholds)."""
+        if isinstance(thresholds, (list, tuple)):
+            tkey = tuple(float(v) for v in thresholds)
+        elif thresholds is not None:
+            thresholds = torch.as_tensor(thresholds, dtype=torch.float32,
+                                         device=self.device).contiguous()
+            tkey = (thresholds.data_ptr(), tuple(thresholds.shape))
+        else:
+            tkey = None
+        key = (tuple(x.shape), x.dtype, mode, tkey)
+        g = self._graphs.get(key)
+        if g is None:
+            if len(self._graphs) >= self.max_graphs:
+                self._graphs.pop(next(iter(self._graphs)))
+            static = torch.empty(x.shape, dtype=x.dtype, device=self.device)
+            static.copy_(x)
+            g = HardGraph(self.plan, static, thresholds, mode, tau=self.head.tau)
+            self._graphs[key] = g
+        return g
+
+    def _run(self, x, thresholds=None, mode=0):
+        """Logits of a numpy / host / device batch; host tensors are copied straight
+        into the graph's static input (pinned memory makes that asynchronous)."""
+        was_np = isinstance(x, np.ndarray)
+        t = torch.from_numpy(np.ascontiguousarray(x)) if was_np else x
+        if self.graphs and t.shape[0] > 0:
+            g = self._graph_for(t, thresholds, mode)
+            g(t)
+            logits = g.logits.clone()
+        else:
+            t = t.to(self.device, non_blocking=True)
+            if thresholds is None:
+                counts = self.plan.counts(t)
+            else:
+                counts = self.plan.counts_from_packed(
+                    _hard.thermo_pack(t, thresholds, mode=mode), t.shape[0])
+            logits = counts.float() / self.head.tau
+        return logits.cpu().numpy() if was_np else logits
 
     def forward(self, x):
-        was_np = isinstance(x, np.ndarray)
-        t = _as_cuda(x)
-        B = t.shape[0]
-        counts = self.plan.counts(t)
-        logits = counts.float() / self.head.tau
-        return logits.cpu().numpy() if was_np else logits
+        return self._run(x)
 
     __call__ = forward
 
@@ -148,11 +196,7 @@ class BitpackedConvNet(BitpackedNet):
         fused into the packing kernel (never materialising the bit planes as bytes).
         ``mode`` 0: shared ``thresholds`` [T] as in ``binarize_spatial``; 1: per-feature
         learned thresholds ``[C*H*W, T]`` as in ``LearnedThermometerEncoder``."""
-        was_np = isinstance(img, np.ndarray)
-        t = _as_cuda(img)
-        h = _hard.thermo_pack(t, thresholds, mode=mode)
-        logits = self.plan.counts_from_packed(h, t.shape[0]).float() / self.head.tau
-        return logits.cpu().numpy() if was_np else logits
+        return self._run(img, thresholds, mode)
 
     @classmethod
     def from_conv_net(cls, bp_conv_net, H_in=None, W_in=None, device="cuda"):

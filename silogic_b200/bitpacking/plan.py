@@ -79,9 +79,59 @@ class HardPlan:
         B = x.shape[0]
         return _hard.groupsum(self.run_packed(self.pack_input(x)), B, self.num_classes)
 
-    def counts_from_packed(self, h, B):
-        return _hard.groupsum(self.run_packed(h), B, self.num_classes)
+    def counts_from_packed(self, h, B, out=None):
+        return _hard.groupsum(self.run_packed(h), B, self.num_classes, out=out)
 
     def features(self, x):
         """Last-layer bits ``[B, width]`` uint8."""
         return _hard.unpack(self.run_packed(self.pack_input(x)), x.shape[0])
+
+
+class HardGraph:
+    """One batch shape of a :class:`HardPlan` captured as a CUDA graph.
+
+    Packing (or the fused thermometer packing), every layer and GroupSum replay as
+    one graph launch, so batches whose kernels last a few microseconds are not bound
+    by the host's per-kernel launch cost.  ``x`` is the graph's static input: pass
+    the tensor that will hold every batch (it is used in place, not copied), or any
+    tensor of the right shape and copy batches in with :meth:`__call__`.  ``out``
+    optionally names the int32 ``[B, num_classes]`` counts buffer to fill.
+    ``thresholds`` / ``mode`` select thermometer input as in ``_hard.thermo_pack``
+    (``None``: ``x`` is already binary).  ``tau`` adds a float32 ``logits`` output
+    ``counts / tau`` to the graph.
+    """
+
+    def __init__(self, plan, x, thresholds=None, mode=0, out=None, tau=None):
+        self.plan, self.x, self.thresholds, self.mode, self.tau = plan, x, thresholds, mode, tau
+        self._out = out
+        dev = x.device
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):      # warm-up: caches thresholds, kernel attributes
+            self._body()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.counts, self.logits = self._body()
+
+    def _body(self):
+        B = self.x.shape[0]
+        if self.thresholds is None:
+            h = self.plan.pack_input(self.x)
+        else:
+            h = _hard.thermo_pack(self.x, self.thresholds, mode=self.mode)
+        counts = self.plan.counts_from_packed(h, B, out=self._out)
+        logits = counts.float() / self.tau if self.tau is not None else None
+        return counts, logits
+
+    def replay(self):
+        self.graph.replay()
+        return self.counts
+
+    def __call__(self, x):
+        """Copy ``x`` (device or pinned host tensor) into the static input and replay."""
+        if x is not self.x:
+            self.x.copy_(x, non_blocking=True)
+        self.graph.replay()
+        return self.counts

@@ -203,54 +203,123 @@ conv_hard_kernel(const uint4* __restrict__ x, int64_t cin, int H, int W, int64_t
 }
 
 // --------------------------------------------------------------- GroupSum
-// CTA = one class x 32 consecutive 32-bit words (1024 samples); its 8 warps split
-// the class's G rows into 8 segments.  Each thread keeps bit-sliced vertical
-// counters for its word (plane l = bit l of every sample's running count), so
-// adding a row is a short carry ripple over LEVELS planes instead of 32
-// per-sample adds; the 8 segment counts are then summed through shared memory.
-constexpr int GS_SEG = 8;
+// CTA = one class x 8 vectors of 128 samples (1024 samples).  Lane = (row segment
+// lane/8, vector lane%8): the 8 warps split the class's G rows into 32 segments of
+// `per` rows (a multiple of 8).  Every count stays bit-sliced (plane l holds bit l
+// of the count of each of 32 samples) from the first row to the last reduction:
+//   rows   -> carry-save adder tree over blocks of 8 rows (Harley-Seal: 7 CSAs per
+//             block and word, the block's "eights" carry rippled into planes 3..),
+//   segments in a warp -> two shuffle rounds of a bit-sliced ripple adder,
+//   warps  -> warp 0 adds the 8 warp sums from shared memory,
+// and only the final planes are turned into one integer per sample.
+constexpr int GS_SEG = 32;
+
+__device__ __forceinline__ void gs_csa(uint32_t& hi, uint32_t& lo, uint32_t a, uint32_t b, uint32_t c) {
+    const uint32_t u = a ^ b;
+    hi = (a & b) | (u & c);
+    lo = u ^ c;
+}
+
+// a += b for two LT-plane bit-sliced numbers (2 three-input logic ops per plane).
+template <int LT>
+__device__ __forceinline__ void gs_add(uint32_t (&a)[LT], const uint32_t (&b)[LT]) {
+    uint32_t c = 0;
+#pragma unroll
+    for (int l = 0; l < LT; ++l) {
+        const uint32_t x = a[l], y = b[l];
+        a[l] = x ^ y ^ c;
+        c = (x & y) | (c & (x ^ y));
+    }
+}
 
 template <int LEVELS>
 __global__ void __launch_bounds__(256)
-groupsum_kernel(const uint32_t* __restrict__ x, int64_t G, int64_t ld32, int64_t B, int C,
-                int32_t* __restrict__ counts) {
-    __shared__ int32_t cnt[GS_SEG][1024 + 8];
-    const int lane = threadIdx.x & 31, seg = threadIdx.x >> 5;
+groupsum_kernel(const uint4* __restrict__ x, int64_t G, int64_t rows_per_split, int64_t per,
+                int64_t nvec, int64_t B, int C, int32_t* __restrict__ counts) {
+    constexpr int LT = LEVELS + 5;   // 32 segments add 5 bits
+    __shared__ uint32_t s_warp[8][32][LT];
+    __shared__ uint32_t s_fin[32][LT + 1];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int vl = lane & 7, seg = warp * 4 + (lane >> 3);
     const int c = blockIdx.y;
-    const int64_t w = (int64_t)blockIdx.x * 32 + lane;
-    const int64_t per = (G + GS_SEG - 1) / GS_SEG;
-    const int64_t g0 = seg * per, g1 = min(G, g0 + per);
-    uint32_t plane[LEVELS];
+    const int64_t v = (int64_t)blockIdx.x * 8 + vl;
+    const int64_t r0 = (int64_t)blockIdx.z * rows_per_split;
+    const int64_t g0 = r0 + seg * per, g1 = min(min(G, r0 + rows_per_split), g0 + per);
+    uint32_t pl[4][LT];
 #pragma unroll
-    for (int l = 0; l < LEVELS; ++l) plane[l] = 0;
-    if (w * 32 < B) {
-        const uint32_t* base = x + (int64_t)c * G * ld32 + w;
-#pragma unroll 4
-        for (int64_t g = g0; g < g1; ++g) {
-            uint32_t carry = __ldg(base + g * ld32);
+    for (int q = 0; q < 4; ++q)
 #pragma unroll
-            for (int l = 0; l < LEVELS; ++l) {
-                const uint32_t t = plane[l] & carry;
-                plane[l] ^= carry;
-                carry = t;
+        for (int l = 0; l < LT; ++l) pl[q][l] = 0;
+    if (v < nvec) {
+        const uint4* base = x + (int64_t)c * G * nvec + v;
+        for (int64_t g = g0; g < g1; g += 8) {
+            uint4 d[8];
+#pragma unroll
+            for (int r = 0; r < 8; ++r)
+                d[r] = (g + r < g1) ? __ldg(base + (g + r) * nvec) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint32_t t2a, t2b, t4a, t4b, t8;
+                uint32_t& ones = pl[q][0];
+                uint32_t& twos = pl[q][1];
+                uint32_t& fours = pl[q][2];
+                gs_csa(t2a, ones, ones, u4get(d[0], q), u4get(d[1], q));
+                gs_csa(t2b, ones, ones, u4get(d[2], q), u4get(d[3], q));
+                gs_csa(t4a, twos, twos, t2a, t2b);
+                gs_csa(t2a, ones, ones, u4get(d[4], q), u4get(d[5], q));
+                gs_csa(t2b, ones, ones, u4get(d[6], q), u4get(d[7], q));
+                gs_csa(t4b, twos, twos, t2a, t2b);
+                gs_csa(t8, fours, fours, t4a, t4b);
+#pragma unroll
+                for (int l = 3; l < LEVELS; ++l) {
+                    const uint32_t t = pl[q][l] & t8;
+                    pl[q][l] ^= t8;
+                    t8 = t;
+                }
             }
         }
     }
-#pragma unroll 4
-    for (int s = 0; s < 32; ++s) {
-        int32_t v = 0;
+    // segments of one warp: lanes l, l^8, l^16, l^24 hold the same words
 #pragma unroll
-        for (int l = 0; l < LEVELS; ++l) v |= (int32_t)((plane[l] >> s) & 1u) << l;
-        cnt[seg][lane * 32 + s] = v;
+    for (int off = 8; off <= 16; off <<= 1)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint32_t o[LT];
+#pragma unroll
+            for (int l = 0; l < LT; ++l) o[l] = __shfl_xor_sync(0xffffffffu, pl[q][l], off);
+            gs_add<LT>(pl[q], o);
+        }
+    if (lane < 8)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int l = 0; l < LT; ++l) s_warp[warp][lane * 4 + q][l] = pl[q][l];
+    __syncthreads();
+    if (warp == 0) {   // lane = word (vector lane/4, component lane%4)
+        uint32_t acc[LT], o[LT];
+#pragma unroll
+        for (int l = 0; l < LT; ++l) acc[l] = s_warp[0][lane][l];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) {
+#pragma unroll
+            for (int l = 0; l < LT; ++l) o[l] = s_warp[w][lane][l];
+            gs_add<LT>(acc, o);
+        }
+#pragma unroll
+        for (int l = 0; l < LT; ++l) s_fin[lane][l] = acc[l];
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < 1024; i += 256) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int i = threadIdx.x + 256 * k;   // sample within the CTA's 1024
         const int64_t b = (int64_t)blockIdx.x * 1024 + i;
         if (b >= B) continue;
-        int32_t v = 0;
+        const int wd = i >> 5, bit = i & 31;
+        int32_t sum = 0;
 #pragma unroll
-        for (int q = 0; q < GS_SEG; ++q) v += cnt[q][i];
-        counts[b * C + c] = v;
+        for (int l = 0; l < LT; ++l) sum |= (int32_t)((s_fin[wd][l] >> bit) & 1u) << l;
+        if (gridDim.z == 1) counts[b * C + c] = sum;
+        else atomicAdd(counts + b * C + c, sum);
     }
 }
 
@@ -354,16 +423,29 @@ extern "C" int slg_groupsum(const uint64_t* x, int64_t width, int64_t ldw, int64
     if (ldw < cdiv(B, 64)) return set_error(SLG_ERR_ARG, "slg_groupsum: ldw too small");
     const int64_t G = width / num_classes;
     if (G >= (1ll << 20)) return set_error(SLG_ERR_UNSUPPORTED, "slg_groupsum: group too large");
+    if (ldw & 1) return set_error(SLG_ERR_ALIGN, "slg_groupsum: ldw must be even");
+    if (!aligned16(x)) return set_error(SLG_ERR_ALIGN, "slg_groupsum: x not 16-byte aligned");
     if (cdiv(B, 1024) > 0x7fffffffLL || num_classes > 65535)
         return set_error(SLG_ERR_ARG, "slg_groupsum: grid too large");
     if (B == 0) return SLG_OK;
     if (!x || !counts) return set_error(SLG_ERR_ARG, "slg_groupsum: null pointer");
-    dim3 grid((unsigned)cdiv(B, 1024), (unsigned)num_classes);
-    const int64_t per = cdiv(G, GS_SEG);   // rows per segment -> counter planes needed
-    auto xs = reinterpret_cast<const uint32_t*>(x);
+    const int64_t nvec = ldw / 2;
+    dim3 grid((unsigned)cdiv(nvec, 8), (unsigned)num_classes);
+    // Small batches give few CTAs: split the rows of each class over grid.z (at least
+    // 256 rows per split) and accumulate with atomics into zeroed counts.
+    int64_t splits = 1;
+    const int64_t ctas = (int64_t)grid.x * grid.y;
+    if (ctas < 2 * sm_count()) splits = std::max<int64_t>(1, std::min(cdiv(2 * sm_count(), ctas), G / 256));
+    const int64_t rps = cdiv(G, splits);
+    splits = cdiv(G, rps);
+    grid.z = (unsigned)splits;
+    const int64_t per = cdiv(cdiv(rps, GS_SEG), 8) * 8;   // rows per segment
+    auto xs = reinterpret_cast<const uint4*>(x);
     cudaStream_t st = as_stream(stream);
-    if (per < (1 << 8)) groupsum_kernel<8><<<grid, 256, 0, st>>>(xs, G, ldw * 2, B, num_classes, counts);
-    else if (per < (1 << 12)) groupsum_kernel<12><<<grid, 256, 0, st>>>(xs, G, ldw * 2, B, num_classes, counts);
-    else groupsum_kernel<17><<<grid, 256, 0, st>>>(xs, G, ldw * 2, B, num_classes, counts);
+    if (splits > 1 && cudaMemsetAsync(counts, 0, sizeof(int32_t) * B * num_classes, st) != cudaSuccess)
+        return check_launch("slg_groupsum");
+    if (per < (1 << 6)) groupsum_kernel<6><<<grid, 256, 0, st>>>(xs, G, rps, per, nvec, B, num_classes, counts);
+    else if (per < (1 << 10)) groupsum_kernel<10><<<grid, 256, 0, st>>>(xs, G, rps, per, nvec, B, num_classes, counts);
+    else groupsum_kernel<16><<<grid, 256, 0, st>>>(xs, G, rps, per, nvec, B, num_classes, counts);
     return check_launch("slg_groupsum");
 }

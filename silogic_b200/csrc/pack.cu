@@ -89,6 +89,56 @@ pack_vec_kernel(const T* __restrict__ x, int64_t B, int64_t F, uint64_t* __restr
     if (myf >= 0 && f0 + myf < F) out[(f0 + myf) * ldw + w] = mine;
 }
 
+// 32x32 bit transpose across a warp: on entry lane l holds row l (bit t = M[l][t]);
+// on exit lane t holds column t (bit l = M[l][t]).  Five block-swap stages.
+__device__ __forceinline__ uint32_t warp_transpose32(uint32_t x, int lane) {
+    const uint32_t masks[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+    for (int s = 0; s < 5; ++s) {
+        const int j = 16 >> s;
+        const uint32_t m = masks[s];
+        const uint32_t other = __shfl_xor_sync(0xffffffffu, x, j);
+        x = (lane & j) ? ((x & ~m) | ((other & ~m) >> j)) : ((x & m) | ((other & m) << j));
+    }
+    return x;
+}
+
+// uint8 packing by warp bit-transpose: lane l loads 32 consecutive feature bytes of
+// sample b0+l (one full 32-byte sector), turns them into a 32-bit nonzero mask, and a
+// warp transpose hands lane f the 32-sample word of feature f0+f.  Two halves give the
+// 64-sample word.  Needs F % 16 == 0 and x 16-byte aligned (the dispatcher checks); a
+// last group of 16 features loads one 16-byte half.
+__global__ void __launch_bounds__(256)
+pack_u8_transpose_kernel(const uint8_t* __restrict__ x, int64_t B, int64_t F, uint64_t* __restrict__ out,
+                         int64_t ldw) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp_id = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nf = (F + 31) / 32;                     // 32-feature groups
+    const int64_t w = warp_id / nf, fg = warp_id % nf;    // 64-sample word, feature group
+    if (w * 64 >= B) return;
+    uint32_t half[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int64_t b = w * 64 + h * 32 + lane;
+        uint32_t m = 0;
+        if (b < B) {
+            const uint4* src = reinterpret_cast<const uint4*>(x + b * F + fg * 32);
+            const uint4 a = __ldg(src);
+            const uint4 c = (fg * 32 + 32 <= F) ? __ldg(src + 1) : make_uint4(0, 0, 0, 0);
+            const uint32_t wv[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const uint32_t v = wv[q];
+                // bit per nonzero byte: 4 bits from this word, at positions 4q..4q+3
+                m |= (uint32_t)((v & 0xffu) != 0) << (4 * q) | (uint32_t)((v & 0xff00u) != 0) << (4 * q + 1) |
+                     (uint32_t)((v & 0xff0000u) != 0) << (4 * q + 2) | (uint32_t)((v >> 24) != 0) << (4 * q + 3);
+            }
+        }
+        half[h] = warp_transpose32(m, lane);
+    }
+    if (fg * 32 + lane < F) out[(fg * 32 + lane) * ldw + w] = ((uint64_t)half[1] << 32) | half[0];
+}
+
 // zero the padding words [nw_valid, ldw) of every row
 __global__ void zero_tail_kernel(uint64_t* out, int64_t rows, int64_t ldw, int64_t nw_valid) {
     int64_t tail = ldw - nw_valid;
@@ -102,20 +152,6 @@ __global__ void unpack_kernel(const uint64_t* __restrict__ p, int64_t F, int64_t
     if (i >= B * F) return;
     int64_t b = i / F, f = i % F;
     out[i] = (uint8_t)((p[f * ldw + (b >> 6)] >> (b & 63)) & 1ull);
-}
-
-// 32x32 bit transpose across a warp: on entry lane l holds row l (bit t = M[l][t]);
-// on exit lane t holds column t (bit l = M[l][t]).  Five block-swap stages.
-__device__ __forceinline__ uint32_t warp_transpose32(uint32_t x, int lane) {
-    const uint32_t masks[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
-#pragma unroll
-    for (int s = 0; s < 5; ++s) {
-        const int j = 16 >> s;
-        const uint32_t m = masks[s];
-        const uint32_t other = __shfl_xor_sync(0xffffffffu, x, j);
-        x = (lane & j) ? ((x & ~m) | ((other & ~m) >> j)) : ((x & m) | ((other & m) << j));
-    }
-    return x;
 }
 
 // Thermometer: x [B, C, HW] -> out [C*T, HW, ldw]
@@ -206,7 +242,11 @@ static int launch_pack(const T* x, int64_t B, int64_t F, uint64_t* out, int64_t 
     if (!x || !out) return set_error(SLG_ERR_ARG, "%s: null pointer", name);
     if (nw > 65535) return set_error(SLG_ERR_ARG, "%s: batch too large (%lld words)", name, (long long)nw);
     dim3 grid((unsigned)cdiv(F, PK_FT), (unsigned)nw);
-    if ((F * (int64_t)sizeof(T)) % 16 == 0 && aligned16(x))
+    if (sizeof(T) == 1 && F % 16 == 0 && aligned16(x)) {
+        const int64_t warps = nw * ((F + 31) / 32);
+        pack_u8_transpose_kernel<<<(unsigned)cdiv(warps * 32, 256), 256, 0, as_stream(stream)>>>(
+            reinterpret_cast<const uint8_t*>(x), B, F, out, ldw);
+    } else if ((F * (int64_t)sizeof(T)) % 16 == 0 && aligned16(x))
         pack_vec_kernel<T, Pred><<<grid, PK_THREADS, 0, as_stream(stream)>>>(x, B, F, out, ldw);
     else
         pack_kernel<T, Pred><<<grid, PK_THREADS, 0, as_stream(stream)>>>(x, B, F, out, ldw);

@@ -205,3 +205,52 @@ def test_thermometer_pack_sorted_unsorted_and_long_vs_oracle(th):
     np.testing.assert_array_equal(got, ref)
     h2 = _hard.thermo_pack(img.cuda(), torch.tensor(th).cuda())      # tensor thresholds path
     np.testing.assert_array_equal(h2.cpu().numpy(), h.cpu().numpy())
+
+
+def test_cuda_graph_replay_matches_eager_and_oracle():
+    """BitpackedNet replays a cached CUDA graph per batch shape; every input form
+    (device, pinned host, numpy, a second batch through the same graph, ragged
+    shapes that evict older graphs) gives the oracle's counts."""
+    from silogic_b200.bitpacking import convert_logic_net
+    kw = dict(node="walsh", connectome="topk", k=8, tau=10.0)
+    m = _rand_fc(100, 300, 3, 11, **kw)
+    sd = {k: v.numpy() for k, v in m.state_dict().items()}
+    bp = convert_logic_net(m.to(dev))
+    bp.max_graphs = 2
+    for i, B in enumerate([129, 129, 64, 3000, 129]):
+        x = (torch.rand(B, 100, generator=torch.Generator().manual_seed(i)) < 0.3).to(torch.uint8)
+        ref = OH.model_counts("LogicNet", dict(in_dim=100, width=300, depth=3, seed=11, **kw), sd,
+                              x.numpy())
+        for xin in (x.cuda(), x.pin_memory(), x.numpy()):
+            got = bp(xin)
+            got = got if isinstance(got, np.ndarray) else got.cpu().numpy()
+            np.testing.assert_array_equal(np.rint(got * 10.0), ref)
+    assert len(bp._graphs) <= 2
+    bp.graphs = False                                      # eager path, same answers
+    np.testing.assert_array_equal(np.rint(bp(x.numpy()) * 10.0), ref)
+
+
+def test_cuda_graph_thermometer_learned_and_shared():
+    """forward_images through the graph cache: shared (mode 0) and learned per-feature
+    (mode 1) thresholds, against the eager path."""
+    import silogic_b200 as S
+    from silogic_b200.bitpacking import convert_logic_conv_net
+    kw = dict(in_channels=15, in_hw=8, channels=[16, 24], head_widths=[60], tree_depth=2,
+              node="gate16", tau=4.0, seed=5)
+    torch.manual_seed(3)
+    m = S.LogicTreeNet(**kw)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.normal_()
+    bp = convert_logic_conv_net(m.cuda())
+    img = torch.rand(77, 3, 8, 8, generator=torch.Generator().manual_seed(6))
+    th = [0.2, 0.4, 0.5, 0.6, 0.8]
+    a = bp.forward_images(img.cuda(), th)
+    bp.graphs = False
+    b = bp.forward_images(img.cuda(), th)
+    np.testing.assert_array_equal(a.cpu().numpy(), b.cpu().numpy())
+    thr = torch.rand(3 * 8 * 8, 5, generator=torch.Generator().manual_seed(7)).cuda()
+    b = bp.forward_images(img.cuda(), thr, mode=1)
+    bp.graphs = True
+    a = bp.forward_images(img.pin_memory(), thr, mode=1)
+    np.testing.assert_array_equal(a.cpu().numpy(), b.cpu().numpy())
