@@ -19,7 +19,7 @@ soft fwd+bwd leg (key "soft_fwd_bwd") is one forward + backward of its batch,
 plus one NCCL all-reduce of the parameter gradients when N > 1.  Hard inference
 shards the batch and all-gathers only the class counts.
 Timing: CUDA events on the launching stream around each step, L2 flushed (a
-256 MB write, untimed) before each step, W >= 3 warm-up steps, barrier +
+256 MB write read back, untimed) before each step, W >= 3 warm-up steps, barrier +
 synchronize around the timed loop, max over ranks.  "e2e" runs the same work
 through the public API from pinned host memory with the host<->device copies
 inside the timed region.
@@ -143,6 +143,14 @@ class ClockSampler:
                           if len(r) > 3 + i and r[3 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(self.rows)}
+
+
+def flush_l2(buf):
+    """Evict the step's data from L2 before a timed step: write a buffer larger than L2,
+    then read it back, so L2 ends up holding clean lines of the flush buffer and the
+    step does not pay for writing back the flush's own dirty lines."""
+    buf.fill_(1)
+    buf.sum()
 
 
 def soak_until_sampled(step, clk, min_s=1.0, min_samples=4):
@@ -333,7 +341,7 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_push("timed_hard")
         for _ in range(steps):
-            flush.fill_(1)
+            flush_l2(flush)
             e0, e1 = events()
             e0.record()
             step_device()
@@ -344,7 +352,7 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
         ms = statistics.mean(a.elapsed_time(b) for a, b in times)
         e2e_times = []
         for _ in range(steps):
-            flush.fill_(1)
+            flush_l2(flush)
             e0, e1 = events()
             e0.record()
             step_e2e()
@@ -358,7 +366,7 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
     step_eager()                # allocator warm-up for the eager pass
     torch.cuda.synchronize()
     for _ in range(steps):      # per-kernel durations, outside the headline region
-        flush.fill_(1)
+        flush_l2(flush)
         step_eager(record=True)
     torch.cuda.synchronize()
     kern = {k: (sum(a.elapsed_time(b) for a, b in v) / steps, len(v) / steps) for k, v in timers.items()}
@@ -411,7 +419,7 @@ def run_soft(cfg, B, steps, warmup, rank, ws, dev):
     times = []
     torch.cuda.nvtx.range_push("timed_soft")
     for _ in range(steps):
-        flush.fill_(1)
+        flush_l2(flush)
         e0, e1 = events()
         e0.record()
         step()
@@ -539,7 +547,7 @@ def main():
             "data": "synthetic (seeded inputs, N(0,1) parameters)",
             "config": {"workload": cfg["name"], "batch_per_gpu": B, "global_batch": total,
                        "parallelism": f"batch shard x{ws}, counts all-gathered",
-                       "l2": "flushed (256 MB write) before each step",
+                       "l2": "flushed before each step (256 MB write, then read back so L2 is clean)",
                        "launch": "one CUDA graph per chunk shape (pack + every layer + GroupSum)",
                        "clocks": "sampled over >= 1 s of untimed replays of the same step, then the timed steps"},
             "e2e": {"value": total / (e2e_ms * 1e-3), "unit": "samples/s",

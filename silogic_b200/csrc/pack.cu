@@ -155,78 +155,129 @@ __global__ void unpack_kernel(const uint64_t* __restrict__ p, int64_t F, int64_t
 }
 
 // Thermometer: x [B, C, HW] -> out [C*T, HW, ldw]
-// tile: 64 samples x PK_FT pixel-features (feature f = c*HW + p), float4 loads when
-// rows allow.  For one feature, lane l builds the thermometer code of samples l and
-// 32+l (bit t = 1[x passes threshold t]) -- by binary search when the shared
-// thresholds are sorted -- and a warp bit-transpose hands lane t the 64-sample word
-// of threshold t, so T words cost ~2 transposes instead of 2T ballots.
-__global__ void __launch_bounds__(PK_THREADS)
+// CTA = 256 samples (4 output words, so every output row gets a whole 32-byte sector
+// from one CTA) x TH_FT pixel-features (feature f = c*HW + p), staged in shared memory
+// with 16-byte loads.  For a threshold chunk of nt <= 32 thresholds, GRP = 32 / nt
+// features share one 32-bit code per sample (bits i*nt + t = 1[x_i passes threshold t];
+// by binary search when the shared thresholds are sorted), and one warp bit-transpose
+// hands lane i*nt + t the 32-sample word of (feature i, threshold t): a warp item
+// (feature group, output word) costs two transposes for up to 32 output words.
+constexpr int TH_FT = 32;
+constexpr int TH_S = 256;
+
+// LOG > 0: shared thresholds sorted ascending, searched in LOG fixed steps over the
+// chunk padded with +inf (count of thresholds <= v, then a thermometer mask);
+// LOG == 0: one comparison per threshold (unsorted shared, or learned per feature).
+template <int LOG>
+__global__ void __launch_bounds__(256)
 thermo_kernel(const float* __restrict__ x, int64_t B, int64_t C, int64_t HW,
-              const float* __restrict__ thr, int T, int mode, int sorted,
+              const float* __restrict__ thr, int T, int mode,
               uint64_t* __restrict__ out, int64_t ldw) {
-    __shared__ float tile[64][PK_FT + 1];
-    __shared__ float sthr[32];
+    __shared__ float tile[TH_S][TH_FT + 1];
+    __shared__ float sthr[TH_FT][33];      // mode 0: row 0 only; mode 1: per feature
+    __shared__ float s_srt[64];            // sorted chunk, padded with +inf
+    __shared__ int64_t s_row[TH_FT];       // pixel p of each feature
+    __shared__ int32_t s_c[TH_FT];         // channel c of each feature
     const int64_t F = C * HW;
-    const int64_t w = blockIdx.y;
-    const int64_t f0 = (int64_t)blockIdx.x * PK_FT;
-    const int64_t b0 = w * 64;
+    const int64_t f0 = (int64_t)blockIdx.x * TH_FT;
+    const int64_t w0 = (int64_t)blockIdx.y * 4;
+    const int64_t b0 = w0 * 64;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const bool vec = (F % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
-    if (vec) {
-        for (int i = threadIdx.x; i < 64 * (PK_FT / 4); i += PK_THREADS) {
-            const int s = i / (PK_FT / 4), q = (i % (PK_FT / 4)) * 4;
-            const int64_t b = b0 + s, ff = f0 + q;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (b < B && ff + 4 <= F) v = __ldg(reinterpret_cast<const float4*>(x + b * F + ff));
-            else if (b < B)
-                for (int e = 0; e < 4; ++e) if (ff + e < F) (&v.x)[e] = x[b * F + ff + e];
-            tile[s][q] = v.x; tile[s][q + 1] = v.y; tile[s][q + 2] = v.z; tile[s][q + 3] = v.w;
+    if (threadIdx.x < TH_FT) {
+        const int64_t ff = f0 + threadIdx.x;
+        const int64_t c = ff / HW, p = ff - c * HW;
+        s_c[threadIdx.x] = (int32_t)c;
+        s_row[threadIdx.x] = p;
+    }
+    if (vec && f0 + TH_FT <= F) {
+        // all 8 16-byte loads of this thread in flight before the shared stores
+        constexpr int N = TH_S * (TH_FT / 4) / 256;
+        float4 r[N];
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+            const int i = threadIdx.x + 256 * k;
+            const int64_t b = b0 + i / (TH_FT / 4);
+            r[k] = b < B ? __ldg(reinterpret_cast<const float4*>(x + b * F + f0 + (i % (TH_FT / 4)) * 4))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+            const int i = threadIdx.x + 256 * k;
+            const int sr = i / (TH_FT / 4), q = (i % (TH_FT / 4)) * 4;
+            tile[sr][q] = r[k].x; tile[sr][q + 1] = r[k].y; tile[sr][q + 2] = r[k].z; tile[sr][q + 3] = r[k].w;
         }
     } else {
-        for (int i = threadIdx.x; i < 64 * PK_FT; i += PK_THREADS) {
-            const int s = i / PK_FT, f = i % PK_FT;
-            const int64_t b = b0 + s, ff = f0 + f;
-            tile[s][f] = (b < B && ff < F) ? x[b * F + ff] : 0.0f;
+        for (int i = threadIdx.x; i < TH_S * TH_FT; i += 256) {
+            const int sr = i / TH_FT, f = i % TH_FT;
+            const int64_t b = b0 + sr, ff = f0 + f;
+            tile[sr][f] = (b < B && ff < F) ? x[b * F + ff] : 0.0f;
         }
     }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t lo_ok = __ballot_sync(0xffffffffu, b0 + lane < B);
-    const uint32_t hi_ok = __ballot_sync(0xffffffffu, b0 + 32 + lane < B);
-    const int per = PK_FT / (PK_THREADS / 32);
+    const int nf = (int)min((int64_t)TH_FT, F - f0);
     for (int t0 = 0; t0 < T; t0 += 32) {
         const int nt = min(32, T - t0);
+        const int grp = 32 / nt;
+        const int ngroups = (nf + grp - 1) / grp;
+        const uint32_t tmask = nt == 32 ? 0xffffffffu : ((1u << nt) - 1u);
+        // this lane's (feature within group, threshold) after the transpose
+        const int li = lane / nt, lt = lane - li * nt;
         __syncthreads();
-        if (mode == 0 && threadIdx.x < nt) sthr[threadIdx.x] = thr[t0 + threadIdx.x];
+        if (mode == 0) {
+            if (threadIdx.x < 32) sthr[0][threadIdx.x] = threadIdx.x < nt ? thr[t0 + threadIdx.x] : 0.0f;
+            if (threadIdx.x < 64) s_srt[threadIdx.x] = threadIdx.x < nt ? thr[t0 + threadIdx.x] : __int_as_float(0x7f800000);
+        } else {
+            for (int i = threadIdx.x; i < TH_FT * nt; i += 256) {
+                const int f = i / nt, t = i % nt;
+                sthr[f][t] = (f0 + f < F) ? thr[(f0 + f) * T + t0 + t] : 0.0f;
+            }
+        }
         __syncthreads();
-        for (int j = 0; j < per; ++j) {
-            const int f = warp * per + j;
-            const int64_t ff = f0 + f;
-            if (ff >= F) break;  // warp-uniform
-            const int64_t c = ff / HW, p = ff % HW;
-            const float v0 = tile[lane][f], v1 = tile[32 + lane][f];
-            uint32_t m0 = 0, m1 = 0;
-            if (mode == 0 && sorted) {
-                int lo0 = 0, hi0 = nt, lo1 = 0, hi1 = nt;      // count of thresholds <= v
+        for (int item = warp; item < ngroups * 2; item += 8) {
+            const int g = item >> 1, wp = item & 1;       // feature group, word pair
+            const int fa = g * grp;
+            uint32_t code[4] = {0, 0, 0, 0};
+            for (int i = 0; i < grp; ++i) {
+                const int f = fa + i;
+                if (f >= nf) break;                          // warp-uniform
+                float v[4];
 #pragma unroll
-                for (int it = 0; it < 6; ++it) {
-                    if (lo0 < hi0) { const int md = (lo0 + hi0) >> 1; if (v0 >= sthr[md]) lo0 = md + 1; else hi0 = md; }
-                    if (lo1 < hi1) { const int md = (lo1 + hi1) >> 1; if (v1 >= sthr[md]) lo1 = md + 1; else hi1 = md; }
-                }
-                m0 = lo0 >= 32 ? 0xffffffffu : ((1u << lo0) - 1u);
-                m1 = lo1 >= 32 ? 0xffffffffu : ((1u << lo1) - 1u);
-            } else {
-                for (int t = 0; t < nt; ++t) {
-                    const float th = mode == 0 ? sthr[t] : thr[ff * T + t0 + t];
-                    const bool a0 = mode == 0 ? (v0 >= th) : ((v0 - th) > 0.0f);
-                    const bool a1 = mode == 0 ? (v1 >= th) : ((v1 - th) > 0.0f);
-                    m0 |= (uint32_t)a0 << t;
-                    m1 |= (uint32_t)a1 << t;
+                for (int h = 0; h < 4; ++h) v[h] = tile[wp * 128 + h * 32 + lane][f];
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    uint32_t m = 0;
+                    if (LOG > 0) {
+                        int pos = 0;
+#pragma unroll
+                        for (int st = LOG - 1; st >= 0; --st) {
+                            const int np = pos + (1 << st);
+                            if (v[h] >= s_srt[np - 1]) pos = np;
+                        }
+                        m = ((pos >= 32 ? 0xffffffffu : ((1u << pos) - 1u))) & tmask;
+                    } else if (mode == 0) {
+                        for (int t = 0; t < nt; ++t) m |= (uint32_t)(v[h] >= sthr[0][t]) << t;
+                    } else {
+                        for (int t = 0; t < nt; ++t) m |= (uint32_t)((v[h] - sthr[f][t]) > 0.0f) << t;
+                    }
+                    code[h] |= m << (i * nt);
                 }
             }
-            const uint32_t lo = warp_transpose32(m0, lane) & lo_ok;
-            const uint32_t hi = warp_transpose32(m1, lane) & hi_ok;
-            if (lane < nt) {
-                const int64_t ch = mode == 0 ? (int64_t)(t0 + lane) * C + c : c * T + t0 + lane;
-                out[(ch * HW + p) * ldw + w] = ((uint64_t)hi << 32) | lo;
+            uint32_t wd[4];
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                const uint32_t ok = __ballot_sync(0xffffffffu, b0 + wp * 128 + h * 32 + lane < B);
+                wd[h] = warp_transpose32(code[h], lane) & ok;
+            }
+            const int f = fa + li;
+            const int64_t w = w0 + wp * 2;
+            if (li < grp && f < nf) {
+                const int64_t c = s_c[f];
+                const int64_t ch = mode == 0 ? (int64_t)(t0 + lt) * C + c : c * T + t0 + lt;
+                uint64_t* dst = out + (ch * HW + s_row[f]) * ldw + w;
+                const uint64_t lo = ((uint64_t)wd[1] << 32) | wd[0];
+                const uint64_t hi = ((uint64_t)wd[3] << 32) | wd[2];
+                if (w + 2 <= ldw) *reinterpret_cast<uint4*>(dst) = make_uint4((uint32_t)lo, (uint32_t)(lo >> 32), (uint32_t)hi, (uint32_t)(hi >> 32));
+                else if (w < ldw) dst[0] = lo;
             }
         }
     }
@@ -289,16 +340,27 @@ extern "C" int slg_thermo_pack(const float* x, int64_t B, int64_t C, int64_t HW,
     if (B == 0) return SLG_OK;
     int64_t nw = cdiv(B, 64);
     if (ldw < nw) return set_error(SLG_ERR_ARG, "slg_thermo_pack: ldw too small");
-    if (nw > 65535) return set_error(SLG_ERR_ARG, "slg_thermo_pack: batch too large");
     if (!x || !thr || !out) return set_error(SLG_ERR_ARG, "slg_thermo_pack: null pointer");
-    dim3 grid((unsigned)cdiv(C * HW, PK_FT), (unsigned)nw);
-    // mode 2 = mode 0 with thresholds the caller guarantees sorted ascending
-    const int sorted = mode == 2 ? 1 : 0;
-    thermo_kernel<<<grid, PK_THREADS, 0, as_stream(stream)>>>(x, B, C, HW, thr, (int)T, mode == 2 ? 0 : mode,
-                                                             sorted, out, ldw);
-    if (ldw > nw) {
-        int64_t rows = C * T * HW, n = rows * (ldw - nw);
-        zero_tail_kernel<<<(unsigned)cdiv(n, 256), 256, 0, as_stream(stream)>>>(out, rows, ldw, nw);
+    if (cdiv(ldw, 4) > 65535) return set_error(SLG_ERR_ARG, "slg_thermo_pack: ldw too large");
+    // one CTA row per 4 words up to ldw: words past the batch come out zero
+    dim3 grid((unsigned)cdiv(C * HW, TH_FT), (unsigned)cdiv(ldw, 4));
+    // mode 2 = mode 0 with thresholds the caller guarantees sorted ascending: binary
+    // search in ceil(log2(nt + 1)) steps, nt = thresholds per 32-chunk
+    cudaStream_t st = as_stream(stream);
+    if (mode == 2) {
+        const int nt = (int)std::min<int64_t>(T, 32);
+        int lg = 0;
+        while ((1 << lg) < nt + 1) ++lg;       // 2^lg - 1 >= nt
+        switch (lg) {
+            case 1: thermo_kernel<1><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw); break;
+            case 2: thermo_kernel<2><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw); break;
+            case 3: thermo_kernel<3><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw); break;
+            case 4: thermo_kernel<4><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw); break;
+            case 5: thermo_kernel<5><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw); break;
+            default: thermo_kernel<6><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw); break;
+        }
+    } else {
+        thermo_kernel<0><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, mode, out, ldw);
     }
     return check_launch("slg_thermo_pack");
 }
