@@ -10,7 +10,8 @@ import os
 import torch
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_PKG, "libsilogic_b200.so")
+# SILOGIC_B200_LIB points at another build of the same library (e.g. a tuning variant)
+LIB_PATH = os.environ.get("SILOGIC_B200_LIB") or os.path.join(_PKG, "libsilogic_b200.so")
 
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32

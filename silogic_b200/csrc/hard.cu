@@ -10,8 +10,8 @@
 namespace slg {
 
 constexpr int HB_THREADS = 256;
-#ifndef SLG_CONV_VPT
-#define SLG_CONV_VPT 1          // 128-sample vectors per thread in the conv tree kernel
+#ifndef SLG_CONV_PPT
+#define SLG_CONV_PPT 4          // pooled positions per thread in the conv tree kernel
 #endif
 #ifndef SLG_CONV_MINB
 #define SLG_CONV_MINB 4         // minimum resident CTAs per SM requested from the compiler
@@ -94,31 +94,70 @@ __device__ __forceinline__ void decode_tap(int r, int k, int& c, int& dy, int& d
     else { const int kk = k * k; c = r / kk; const int q = r - c * kk; dy = q / k; dx = q - dy * k; }
 }
 
-// One thread: output channel n, one pooled position, VPT vectors of 128 samples.
-// Tap addresses of each pre-pool position are computed once and shared by the
-// thread's vectors.
+// One thread: output channel n (uniform over the CTA), one 128-sample vector, and
+// `ppt` consecutive pooled positions in raster order.  The leaf decode, the truth-table
+// masks and the per-leaf offsets are computed once and reused for every position;
+// positions whose receptive field lies inside the image skip the padding checks.
+// Offsets within one channel plane are 32-bit (H*W*nvec < 2^31, checked by the host).
+template <int AR, int DEPTH, int POOL, bool CHECK>
+__device__ __forceinline__ uint4 conv_tree_at(const uint4* const (&lp)[Tree<AR, DEPTH>::LEAVES],
+                                              const int (&ly)[Tree<AR, DEPTH>::LEAVES],
+                                              const int (&lx)[Tree<AR, DEPTH>::LEAVES],
+                                              const int (&dpn)[Tree<AR, DEPTH>::LEAVES],
+                                              const uint32_t (*mk)[1 << AR], const uint64_t* tn,
+                                              int y, int xx, int H, int W, int nvec) {
+    constexpr int LEAVES = Tree<AR, DEPTH>::LEAVES;
+    constexpr bool PRE = Tree<AR, DEPTH>::NODES * (1 << AR) <= 64;
+    const int pixn = (y * W + xx) * nvec;
+    uint32_t val[LEAVES][4];
+#pragma unroll
+    for (int l = 0; l < LEAVES; ++l) {
+        uint4 t = make_uint4(0, 0, 0, 0);
+        if (!CHECK || ((unsigned)(y + ly[l]) < (unsigned)H && (unsigned)(xx + lx[l]) < (unsigned)W))
+            t = __ldg(lp[l] + (pixn + dpn[l]));
+        val[l][0] = t.x; val[l][1] = t.y; val[l][2] = t.z; val[l][3] = t.w;
+    }
+    int width = LEAVES, node_base = 0;
+#pragma unroll
+    for (int lev = 0; lev < DEPTH; ++lev) {
+        const int nn = width / AR;
+#pragma unroll
+        for (int m = 0; m < nn; ++m) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t vv[AR];
+#pragma unroll
+                for (int j = 0; j < AR; ++j) vv[j] = val[m * AR + j][c];
+                if constexpr (PRE) val[m][c] = lut_eval_m<AR>(vv, mk[node_base + m]);
+                else val[m][c] = lut_eval<AR>(vv, tn[node_base + m]);
+            }
+        }
+        node_base += nn;
+        width = nn;
+    }
+    return make_uint4(val[0][0], val[0][1], val[0][2], val[0][3]);
+}
+
 template <int AR, int DEPTH, int POOL>
-__global__ void __launch_bounds__(HB_THREADS, SLG_CONV_MINB)
-conv_hard_kernel(const uint4* __restrict__ x, int64_t cin, int H, int W, int64_t nvec,
+__global__ void __launch_bounds__(HB_THREADS, (Tree<AR, DEPTH>::LEAVES <= 5 ? SLG_CONV_MINB : 2))
+conv_hard_kernel(const uint4* __restrict__ x, int64_t cin, int H, int W, int nvec,
                  const int32_t* __restrict__ leaf, const uint64_t* __restrict__ tt, int kernel,
                  int pad, int64_t n_out, int64_t wire_r, int Hp, int Wp,
-                 uint4* __restrict__ out, int vt_shift) {
+                 uint4* __restrict__ out, int vt_shift, int ppt) {
     constexpr int LEAVES = Tree<AR, DEPTH>::LEAVES;
     constexpr int NODES = Tree<AR, DEPTH>::NODES;
-    constexpr int VPT = SLG_CONV_VPT;
     const int vt = 1 << vt_shift;
-    const int ppb = HB_THREADS >> vt_shift;         // positions per block
+    const int slots = HB_THREADS >> vt_shift;
     const int npos = Hp * Wp;
-    const int tiles = (npos + ppb - 1) / ppb;
+    const int tiles = (npos + slots * ppt - 1) / (slots * ppt);
     const int64_t n = blockIdx.x / tiles;
-    const int pos = (blockIdx.x % tiles) * ppb + (threadIdx.x >> vt_shift);
-    const int64_t v0 = (int64_t)blockIdx.y * vt * VPT + (threadIdx.x & (vt - 1));
-    if (n >= n_out || pos >= npos || v0 >= nvec) return;
-    const int py = pos / Wp, px = pos - py * Wp;
+    const int pos0 = (blockIdx.x % tiles) * slots * ppt + (threadIdx.x >> vt_shift) * ppt;
+    const int v0 = blockIdx.y * vt + (threadIdx.x & (vt - 1));
+    if (n >= n_out || pos0 >= npos || v0 >= nvec) return;
     const int64_t plane = (int64_t)H * W * nvec;
 
     const uint4* lp[LEAVES];                        // channel plane of each leaf (+ this lane's v)
-    int ly[LEAVES], lx[LEAVES];
+    int ly[LEAVES], lx[LEAVES], dpn[LEAVES];
 #pragma unroll
     for (int l = 0; l < LEAVES; ++l) {
         int c, dy, dx;
@@ -126,6 +165,7 @@ conv_hard_kernel(const uint4* __restrict__ x, int64_t cin, int H, int W, int64_t
         lp[l] = x + c * plane + v0;
         ly[l] = dy - pad;
         lx[l] = dx - pad;
+        dpn[l] = (ly[l] * W + lx[l]) * nvec;
     }
     constexpr bool PRE = NODES * (1 << AR) <= 64;   // leaf masks of every node fit in registers
     uint64_t tn[NODES];
@@ -136,70 +176,38 @@ conv_hard_kernel(const uint4* __restrict__ x, int64_t cin, int H, int W, int64_t
         if constexpr (PRE) lut_masks<AR>(tn[i], mk[i]);
     }
     const bool wired = n < wire_r;
-    int nu = 0;                                     // vectors this thread owns (<= VPT)
+    const int pend = min(npos, pos0 + ppt);
+    int py = pos0 / Wp, px = pos0 - py * Wp;
+    uint4* dst = out + (n * npos + pos0) * (int64_t)nvec + v0;
+    for (int pos = pos0; pos < pend; ++pos) {
+        uint4 acc = make_uint4(0, 0, 0, 0);
+        const int y0 = py * POOL, x0 = px * POOL;
+        if (wired) {
+            const uint4* src = x + n * plane + v0;
 #pragma unroll
-    for (int u = 0; u < VPT; ++u) nu += (v0 + (int64_t)u * vt < nvec) ? 1 : 0;
-    uint4 acc[VPT];
+            for (int oy = 0; oy < POOL; ++oy)
 #pragma unroll
-    for (int u = 0; u < VPT; ++u) acc[u] = make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int oy = 0; oy < POOL; ++oy) {
-#pragma unroll
-        for (int ox = 0; ox < POOL; ++ox) {
-            const int y = py * POOL + oy, xx = px * POOL + ox;
-            if (wired) {
-                const uint4* src = x + n * plane + (int64_t)(y * W + xx) * nvec + v0;
-#pragma unroll
-                for (int u = 0; u < VPT; ++u)
-                    if (u < nu) {
-                        const uint4 t = __ldg(src + (int64_t)u * vt);
-                        acc[u].x |= t.x; acc[u].y |= t.y; acc[u].z |= t.z; acc[u].w |= t.w;
-                    }
-                continue;
-            }
-            const uint4* tp[LEAVES];
-            bool ok[LEAVES];
-#pragma unroll
-            for (int l = 0; l < LEAVES; ++l) {
-                const int iy = y + ly[l], ix = xx + lx[l];
-                ok[l] = (unsigned)iy < (unsigned)H && (unsigned)ix < (unsigned)W;
-                tp[l] = lp[l] + (ok[l] ? (int64_t)(iy * W + ix) * nvec : 0);
-            }
-#pragma unroll
-            for (int u = 0; u < VPT; ++u) {
-                if (u >= nu) break;
-                uint32_t val[LEAVES][4];
-#pragma unroll
-                for (int l = 0; l < LEAVES; ++l) {
-                    uint4 t = make_uint4(0, 0, 0, 0);
-                    if (ok[l]) t = __ldg(tp[l] + (int64_t)u * vt);
-                    val[l][0] = t.x; val[l][1] = t.y; val[l][2] = t.z; val[l][3] = t.w;
+                for (int ox = 0; ox < POOL; ++ox) {
+                    const uint4 t = __ldg(src + ((y0 + oy) * W + x0 + ox) * nvec);
+                    acc.x |= t.x; acc.y |= t.y; acc.z |= t.z; acc.w |= t.w;
                 }
-                int width = LEAVES, node_base = 0;
+        } else {
+            const bool inside = y0 - pad >= 0 && y0 + POOL - 1 + kernel - 1 - pad < H &&
+                                x0 - pad >= 0 && x0 + POOL - 1 + kernel - 1 - pad < W;
 #pragma unroll
-                for (int lev = 0; lev < DEPTH; ++lev) {
-                    const int nn = width / AR;
+            for (int oy = 0; oy < POOL; ++oy)
 #pragma unroll
-                    for (int m = 0; m < nn; ++m) {
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            uint32_t vv[AR];
-#pragma unroll
-                            for (int j = 0; j < AR; ++j) vv[j] = val[m * AR + j][c];
-                            if constexpr (PRE) val[m][c] = lut_eval_m<AR>(vv, mk[node_base + m]);
-                            else val[m][c] = lut_eval<AR>(vv, tn[node_base + m]);
-                        }
-                    }
-                    node_base += nn;
-                    width = nn;
+                for (int ox = 0; ox < POOL; ++ox) {
+                    const uint4 t = inside
+                        ? conv_tree_at<AR, DEPTH, POOL, false>(lp, ly, lx, dpn, mk, tn, y0 + oy, x0 + ox, H, W, nvec)
+                        : conv_tree_at<AR, DEPTH, POOL, true>(lp, ly, lx, dpn, mk, tn, y0 + oy, x0 + ox, H, W, nvec);
+                    acc.x |= t.x; acc.y |= t.y; acc.z |= t.z; acc.w |= t.w;
                 }
-                acc[u].x |= val[0][0]; acc[u].y |= val[0][1]; acc[u].z |= val[0][2]; acc[u].w |= val[0][3];
-            }
         }
+        *dst = acc;
+        dst += nvec;
+        if (++px == Wp) { px = 0; ++py; }
     }
-#pragma unroll
-    for (int u = 0; u < VPT; ++u)
-        if (u < nu) out[(n * npos + pos) * nvec + v0 + (int64_t)u * vt] = acc[u];
 }
 
 // --------------------------------------------------------------- GroupSum
@@ -363,14 +371,15 @@ extern "C" int slg_fc_hard(const uint64_t* x, int64_t in_dim, int64_t ldw, const
 
 template <int AR, int D>
 static void launch_conv(dim3 g, cudaStream_t st, const uint4* x, int64_t cin, int H, int W,
-                        int64_t nvec, const int32_t* leaf, const uint64_t* tt, int kernel, int pad,
-                        int64_t n_out, int64_t wire_r, int pool, int Hp, int Wp, uint4* out, int vs) {
+                        int nvec, const int32_t* leaf, const uint64_t* tt, int kernel, int pad,
+                        int64_t n_out, int64_t wire_r, int pool, int Hp, int Wp, uint4* out, int vs,
+                        int ppt) {
     if (pool == 2)
         conv_hard_kernel<AR, D, 2><<<g, HB_THREADS, 0, st>>>(x, cin, H, W, nvec, leaf, tt, kernel, pad,
-                                                             n_out, wire_r, Hp, Wp, out, vs);
+                                                             n_out, wire_r, Hp, Wp, out, vs, ppt);
     else
         conv_hard_kernel<AR, D, 1><<<g, HB_THREADS, 0, st>>>(x, cin, H, W, nvec, leaf, tt, kernel, pad,
-                                                             n_out, wire_r, Hp, Wp, out, vs);
+                                                             n_out, wire_r, Hp, Wp, out, vs, ppt);
 }
 
 extern "C" int slg_conv_hard(const uint64_t* x, int64_t cin, int64_t H, int64_t W, int64_t ldw,
@@ -390,12 +399,18 @@ extern "C" int slg_conv_hard(const uint64_t* x, int64_t cin, int64_t H, int64_t 
     if (n_out == 0 || Hp == 0 || Wp == 0) return SLG_OK;
     if (!leaf || !tt) return set_error(SLG_ERR_ARG, "slg_conv_hard: null pointer");
     const int64_t nvec = ldw / 2;
-    const int vt = pick_vt(cdiv(nvec, SLG_CONV_VPT));
+    if (H * W * nvec >= (1ll << 31) || Hp * Wp * nvec >= (1ll << 31))
+        return set_error(SLG_ERR_UNSUPPORTED, "slg_conv_hard: channel plane over 2^31 words; split the batch");
+    const int vt = pick_vt(nvec);
     int vs = 0;
     while ((1 << vs) < vt) ++vs;
-    const int64_t ppb = HB_THREADS / vt;
-    const int64_t tiles = cdiv(Hp * Wp, ppb);
-    const int64_t gy = cdiv(nvec, vt * SLG_CONV_VPT);
+    const int64_t slots = HB_THREADS / vt;
+    const int64_t npos = Hp * Wp;
+    // positions per thread: amortise the per-thread setup, but keep >= ~4 waves of CTAs
+    int64_t ppt = std::max<int64_t>(1, std::min<int64_t>(SLG_CONV_PPT, cdiv(npos, slots)));
+    const int64_t gy = cdiv(nvec, vt);
+    while (ppt > 1 && n_out * cdiv(npos, slots * ppt) * gy < 4ll * 4 * sm_count()) ppt >>= 1;
+    const int64_t tiles = cdiv(npos, slots * ppt);
     if (gy > 65535 || n_out * tiles > 0x7fffffffLL || H * W > (1 << 24))
         return set_error(SLG_ERR_ARG, "slg_conv_hard: grid too large");
     dim3 grid((unsigned)(n_out * tiles), (unsigned)gy);
@@ -404,7 +419,7 @@ extern "C" int slg_conv_hard(const uint64_t* x, int64_t cin, int64_t H, int64_t 
     cudaStream_t st = as_stream(stream);
     const int key = arity * 10 + depth;
 #define SLG_CONV_CASE(A, D) \
-    case A * 10 + D: launch_conv<A, D>(grid, st, xs, cin, (int)H, (int)W, nvec, leaf, tt, kernel, pad, n_out, wire_r, pool, (int)Hp, (int)Wp, os, vs); break;
+    case A * 10 + D: launch_conv<A, D>(grid, st, xs, cin, (int)H, (int)W, (int)nvec, leaf, tt, kernel, pad, n_out, wire_r, pool, (int)Hp, (int)Wp, os, vs, (int)ppt); break;
     switch (key) {
         SLG_CONV_CASE(2, 1) SLG_CONV_CASE(2, 2) SLG_CONV_CASE(2, 3) SLG_CONV_CASE(2, 4)
         SLG_CONV_CASE(3, 1) SLG_CONV_CASE(3, 2) SLG_CONV_CASE(4, 1) SLG_CONV_CASE(4, 2)
