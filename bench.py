@@ -274,11 +274,18 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
         timers.setdefault(name, []).append((e0, e1))
         return r
 
+    def uses_chain(n):
+        return plan.use_chain and n >= plan.chain_min_batch and plan.chain() is not None
+
     def step_eager(record=False):
         """Kernel-by-kernel launch of one step (per-kernel timing pass)."""
         for c in range(nchunks):
             n = min(chunk, B - c * chunk)
             h = timed("pack", lambda: pack_chunk(n), record)
+            if uses_chain(n):
+                timed("fc_chain", lambda: plan.chain().counts(h, n, out=counts_all[c * chunk:c * chunk + n]),
+                      record)
+                continue
             for st in plan.steps:
                 hh = h
                 if st["op"] == "fc":
@@ -300,13 +307,12 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
         n = min(chunk, B - c * chunk)
         if n not in graphs:
             graphs[n] = HardGraph(plan, x_dev[:n], graph_thr, mode)
-    kernels_per_chunk = 2 + len(plan.steps)
 
     def step_device(collective=True):
         for c in range(nchunks):
             n = min(chunk, B - c * chunk)
             counts_all[c * chunk:c * chunk + n].copy_(graphs[n].replay())
-            launches[0] += kernels_per_chunk
+            launches[0] += 2 if uses_chain(n) else 2 + len(plan.steps)
         if ws > 1 and collective:   # only the class counts leave the GPU
             torch.distributed.all_gather_into_tensor(gathered, counts_all)
         return counts_all
@@ -374,6 +380,9 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
     per_kind = {}
     for name, bps in stage:
         per_kind[name] = per_kind.get(name, 0.0) + bps
+    # the fused whole-stack kernel is credited with the layer-wise bytes of the
+    # stages it replaces (every FC layer and the GroupSum)
+    per_kind["fc_chain"] = per_kind.get("fc_hard", 0.0) + per_kind.get("groupsum", 0.0)
     in_bytes = x_host[:1].numel() * x_host.element_size()
     return dict(ms=ms, e2e_ms=e2e_ms, kern=kern, per_kind=per_kind,
                 bytes_per_sample=sum(b for _, b in stage), launches_per_step=launches[0] / steps,

@@ -104,6 +104,34 @@ int slg_conv_hard(const uint64_t* x, int64_t cin, int64_t H, int64_t W, int64_t 
 int slg_groupsum(const uint64_t* x, int64_t width, int64_t ldw, int64_t B,
                  int32_t num_classes, int32_t* counts, void* stream);
 
+/* Whole-stack form of the FC hard path for arity-2 circuits (gate16, Walsh, arity-2
+ * multilinear / LUT-2): every layer and the GroupSum in ONE persistent launch, the
+ * activations of each 64-sample column staying in shared memory between layers.
+ * Same results as slg_fc_hard per layer followed by slg_groupsum; replaces the
+ * layer loop of BitpackedNet.forward (silogic/bitpacking/packed_model.py:75-102)
+ * with the head of BitpackedGroupSumHead (packed_layer.py:545-571) as integer counts.
+ *
+ * slg_fc_chain_encode: one layer's wiring idx[out_dim*2] + tables tt[out_dim]
+ *   (wire_r leading residual wires) -> rec[out_dim] 32-bit node records.
+ * slg_fc_chain_counts: x packed [in_dim, ldw]; rec = the layers' records
+ *   concatenated; widths = HOST array of n_layers layer widths (each and in_dim
+ *   <= SLG_CHAIN_MAX_WIDTH); class_off = HOST array of num_classes + 1 row offsets
+ *   into the last layer (class c = rows [off[c], off[c+1])), or NULL for equal
+ *   contiguous blocks; counts[B * num_classes] int32.  A host planner may store
+ *   each layer's nodes in any order (and pad with constant-zero nodes) as long as
+ *   the next layer's records address the stored slots.
+ * slg_fc_chain_smem_bytes: shared memory one CTA needs (2 x max width x 8). */
+#define SLG_CHAIN_MAX_LAYERS 32
+#define SLG_CHAIN_MAX_WIDTH 13824
+#define SLG_CHAIN_MAX_CLASSES 64
+int slg_fc_chain_encode(const int32_t* idx, const uint64_t* tt, int64_t out_dim, int64_t wire_r,
+                        uint32_t* rec, void* stream);
+int64_t slg_fc_chain_smem_bytes(int64_t in_dim, const int32_t* widths, int32_t n_layers);
+int slg_fc_chain_counts(const uint64_t* x, int64_t in_dim, int64_t ldw, int64_t B,
+                        const uint32_t* rec, const int32_t* widths, int32_t n_layers,
+                        int32_t num_classes, const int32_t* class_off, int32_t* counts,
+                        void* stream);
+
 /* ------------------------------------------------------- soft FC layer */
 
 /* Node kinds of the soft kernels. */

@@ -4,6 +4,8 @@ Packed activations are int64 tensors ``[rows, ldw]`` (conv: ``[C, H, W, ldw]``)
 with ``ldw = ceil(B/64)`` rounded up to even; sample ``b`` is bit ``b % 64`` of
 word ``b // 64``, as in ``silogic/bitpacking/ops.py:32-49``.
 """
+import ctypes
+
 import torch
 
 from . import _lib
@@ -132,6 +134,172 @@ def groupsum(x, B, num_classes, out=None):
     call("slg_groupsum", ptr(x), width, x.shape[-1], B, num_classes, ptr(out),
          stream_ptr(x.device))
     return out
+
+
+# ------------------------------------------- whole FC stack in one launch
+CHAIN_MAX_LAYERS = 32
+CHAIN_MAX_WIDTH = 13824
+CHAIN_MAX_CLASSES = 64
+
+
+def chain_encode(idx, tt, wire_r=0):
+    """One arity-2 layer's wiring ``[out, 2]`` + tables ``[out]`` -> ``[out]`` int32 records."""
+    require_cuda(tt)
+    out_dim = tt.shape[0]
+    rec = torch.empty(out_dim, dtype=torch.int32, device=tt.device)
+    call("slg_fc_chain_encode", ptr(idx.contiguous()), ptr(tt.contiguous()), out_dim, wire_r,
+         ptr(rec), stream_ptr(tt.device))
+    return rec
+
+
+def _half_warps(ka, kb, nodes):
+    """Split ``nodes`` into half-warps (<= 16 lanes) whose 64-bit shared loads are free of
+    bank conflicts: within a half-warp every node's first input sits in a distinct
+    8-byte bank pair (``ka``) and so does its second (``kb``).  A half-warp is a
+    matching of the bipartite multigraph bank-pair(a) -- node -- bank-pair(b), so this
+    is a bipartite edge colouring; the alternating-path method (Konig) uses exactly
+    max-degree colours, the fewest possible."""
+    adj = {}                      # (side, bank) -> {colour: node}
+    colour = {}
+
+    def free(v):
+        d = adj.setdefault(v, {})
+        c = 0
+        while c in d:
+            c += 1
+        return c
+
+    for j in nodes:
+        u, v = ("a", ka[j]), ("b", kb[j])
+        du, dv = adj.setdefault(u, {}), adj.setdefault(v, {})
+        al, be = free(u), free(v)
+        if al not in dv:
+            pass
+        else:
+            # swap colours al/be along the alternating path that starts at v with al;
+            # in a bipartite graph it cannot end at u, so al becomes free at v
+            path, x, c = [], v, al
+            while c in adj[x]:
+                e = adj[x][c]
+                path.append(e)
+                y = ("b", kb[e]) if x == ("a", ka[e]) else ("a", ka[e])
+                x, c = y, (be if c == al else al)
+            for e in path:
+                ea, eb = ("a", ka[e]), ("b", kb[e])
+                del adj[ea][colour[e]]
+                del adj[eb][colour[e]]
+            for e in path:
+                colour[e] = be if colour[e] == al else al
+                adj[("a", ka[e])][colour[e]] = e
+                adj[("b", kb[e])][colour[e]] = e
+        colour[j] = al
+        du[al] = j
+        dv[al] = j
+    halves = {}
+    for j in nodes:
+        halves.setdefault(colour[j], []).append(j)
+    return [halves[c] for c in sorted(halves)]
+
+
+def chain_layout(steps, in_dim, num_classes, reorder=True):
+    """Node records, layer widths and class offsets for :class:`FCChain`.
+
+    Each layer's nodes are stored in the order they are processed (lanes of warp ``w``
+    of an iteration handle slots ``32w .. 32w+31``), arranged in half-warps whose
+    lanes read their two inputs from distinct shared-memory bank pairs (no bank
+    conflicts); half-warps are padded to 16 lanes with constant-zero nodes that read
+    a live lane's inputs (a broadcast).  The last layer is arranged per class block so
+    GroupSum reads class ``c`` as slots ``[off[c], off[c+1])`` (padding rows are zero).
+    A layer whose arrangement would exceed the width limit keeps its natural order.
+    Returns ``(records uint32 numpy, widths, class offsets)``; record =
+    in_a | in_b << 14 | table << 28 over storage slots.
+    """
+    import numpy as np
+    pos = np.arange(in_dim)
+    recs, widths = [], []
+    class_off = None
+    for li, st in enumerate(steps):
+        idx = st["idx"].detach().cpu().numpy().astype(np.int64)
+        tt = st["tt"].detach().cpu().numpy().astype(np.int64)
+        out = idx.shape[0]
+        a, b, g = pos[idx[:, 0]], pos[idx[:, 1]], tt & 15
+        wr = int(st["wire_r"])
+        if wr:   # residual wire: identity on the first input (address a + 2b -> 0b1010)
+            a[:wr] = pos[:wr]
+            b[:wr] = pos[:wr]
+            g[:wr] = 0xA
+        node_rec = (a | (b << 14) | (g << 28)).astype(np.uint32)
+        ka, kb = (a % 16).tolist(), (b % 16).tolist()
+        last = li == len(steps) - 1
+        G = out // num_classes
+        blocks = [range(c * G, (c + 1) * G) for c in range(num_classes)] if last else [range(out)]
+        layout = None
+        if reorder:
+            layout = []
+            for blk in blocks:
+                hw = _half_warps(ka, kb, blk)
+                hw += [[]] * (len(hw) % 2)                    # whole warps per block
+                layout.append(hw)
+            if sum(len(h) for h in layout) * 16 > CHAIN_MAX_WIDTH:
+                layout = None
+        if layout is None:   # natural order, blocks padded to whole warps
+            layout = [[list(blk[i:i + 16]) for i in range(0, len(blk), 16)] for blk in blocks]
+            layout = [hw + [[]] * (len(hw) % 2) for hw in layout]
+        width = sum(len(h) for h in layout) * 16
+        slot = np.zeros(out, dtype=np.int64)
+        rec = np.zeros(width, dtype=np.uint32)
+        offs = [0]
+        s0 = 0
+        rot = 0
+        for hw in layout:
+            for half in hw:
+                # live lanes start at a rotating offset so padding does not pile up in
+                # the same bank pairs (which would skew the next layer's reads)
+                lanes = (rot + np.arange(16)) % 16
+                rot = (rot + 16 - len(half)) % 16
+                slot[half] = s0 + lanes[:len(half)]
+                if half and len(half) < 16:
+                    # padding lanes: a live lane's inputs (broadcast), constant-zero table
+                    rec[s0 + lanes[len(half):]] = node_rec[half[0]] & np.uint32(0x0fffffff)
+                s0 += 16
+            offs.append(s0)
+        rec[slot] = node_rec
+        recs.append(rec)
+        widths.append(width)
+        if last:
+            class_off = offs
+        pos = slot
+    return np.concatenate(recs), widths, class_off
+
+
+class FCChain:
+    """Arity-2 FC layers + GroupSum as one persistent kernel (``slg_fc_chain_counts``)."""
+
+    def __init__(self, steps, in_dim, num_classes, device, reorder=True):
+        rec, self.widths, self.class_off = chain_layout(steps, in_dim, num_classes, reorder)
+        self.rec = torch.from_numpy(rec.view("int32")).to(device)
+        self.in_dim, self.num_classes = int(in_dim), int(num_classes)
+        self._w = (ctypes.c_int32 * len(self.widths))(*self.widths)
+        self._off = (ctypes.c_int32 * len(self.class_off))(*self.class_off)
+
+    @staticmethod
+    def supported(steps, in_dim, num_classes):
+        if (not steps or len(steps) > CHAIN_MAX_LAYERS or not num_classes
+                or num_classes > CHAIN_MAX_CLASSES or in_dim > CHAIN_MAX_WIDTH):
+            return False
+        for st in steps:
+            if st["op"] != "fc" or st["idx"].shape[1] != 2 or st["idx"].shape[0] > CHAIN_MAX_WIDTH:
+                return False
+        return steps[-1]["idx"].shape[0] % num_classes == 0
+
+    def counts(self, h, B, out=None):
+        require_cuda(h)
+        if out is None:
+            out = torch.empty((B, self.num_classes), dtype=torch.int32, device=h.device)
+        call("slg_fc_chain_counts", ptr(h), self.in_dim, h.shape[-1], B, ptr(self.rec),
+             ctypes.cast(self._w, ctypes.c_void_p), len(self.widths), self.num_classes,
+             ctypes.cast(self._off, ctypes.c_void_p), ptr(out), stream_ptr(h.device))
+        return out
 
 
 # ------------------------------------------------- parameters -> truth tables

@@ -29,6 +29,8 @@ _SIGS = {
     "slg_conv_hard": [_p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _i64, _i64,
                       _i32, _p, _p],
     "slg_groupsum": [_p, _i64, _i64, _i64, _i32, _p, _p],
+    "slg_fc_chain_encode": [_p, _p, _i64, _i64, _p, _p],
+    "slg_fc_chain_counts": [_p, _i64, _i64, _i64, _p, _p, _i32, _i32, _p, _p, _p],
     "slg_fc_soft_fwd": [_p, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _p, _i32, _f32, _i64,
                         _i64, _p, _p],
     "slg_fc_soft_bwd": [_p, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _p, _i32, _f32, _i64,
@@ -48,6 +50,7 @@ _SIGS = {
 }
 # entry points that do not return a status
 _RESTYPES = {
+    "slg_fc_chain_smem_bytes": ([_i64, _p, _i32], ctypes.c_int64),
     "slg_fc_soft_workspace_bytes": ([_i64, _i32, _i32, _i32, _i64], ctypes.c_int64),
     "slg_conv_soft_workspace_bytes": ([_i64, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                                        _i64], ctypes.c_int64),

@@ -13,11 +13,28 @@ from .. import _hard
 class HardPlan:
     """Wiring + truth tables of every layer, on the parameters' device."""
 
+    #: batches at least this large run an all-FC arity-2 plan as one persistent
+    #: kernel (``_hard.FCChain``: activations stay in shared memory between layers)
+    chain_min_batch = 8192
+
     def __init__(self, steps, in_shape, num_classes, tau):
         self.steps = steps            # list of dicts, see from_model
         self.in_shape = in_shape      # ("fc", F) or ("conv", C, H, W)
         self.num_classes = num_classes
         self.tau = tau
+        self.use_chain = True
+        self._chain = None
+        self._chain_ok = (in_shape[0] == "fc" and
+                          _hard.FCChain.supported(steps, in_shape[1], num_classes))
+
+    def chain(self):
+        """The fused whole-stack kernel for this plan, or None when it does not apply."""
+        if not self._chain_ok:
+            return None
+        if self._chain is None:
+            self._chain = _hard.FCChain(self.steps, self.in_shape[1], self.num_classes,
+                                        self.steps[0]["tt"].device)
+        return self._chain
 
     # ----------------------------------------------------------- building
     @classmethod
@@ -77,9 +94,11 @@ class HardPlan:
     def counts(self, x):
         """Integer GroupSum counts ``[B, num_classes]`` (int32) of binary input ``x``."""
         B = x.shape[0]
-        return _hard.groupsum(self.run_packed(self.pack_input(x)), B, self.num_classes)
+        return self.counts_from_packed(self.pack_input(x), B)
 
     def counts_from_packed(self, h, B, out=None):
+        if self.use_chain and B >= self.chain_min_batch and self.chain() is not None:
+            return self._chain.counts(h, B, out=out)
         return _hard.groupsum(self.run_packed(h), B, self.num_classes, out=out)
 
     def features(self, x):

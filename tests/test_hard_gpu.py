@@ -254,3 +254,41 @@ def test_cuda_graph_thermometer_learned_and_shared():
     bp.graphs = True
     a = bp.forward_images(img.pin_memory(), thr, mode=1)
     np.testing.assert_array_equal(a.cpu().numpy(), b.cpu().numpy())
+
+
+@pytest.mark.parametrize("B", [1, 64, 100, 1000, 4097, 20000])
+@pytest.mark.parametrize("kw", [dict(node="walsh", connectome="topk", k=8, tau=10.0),
+                                dict(node="gate16", connectome="fixed", tau=10.0),
+                                dict(node="gate16", connectome="topk", k=4, tau=10.0,
+                                     wire_residual=0.25),
+                                dict(node="multilinear", connectome="topk", k=8, tau=10.0)])
+def test_fc_chain_whole_stack_kernel_vs_oracle(B, kw):
+    """The one-launch FC stack + GroupSum (slg_fc_chain_counts) == oracle counts."""
+    m = _rand_fc(100, 300, 3, 13, **kw)
+    g = torch.Generator().manual_seed(B)
+    x = (torch.rand(B, 100, generator=g) < 0.3).to(torch.uint8)
+    sd = {k: v.numpy() for k, v in m.state_dict().items()}
+    ref = OH.model_counts("LogicNet", dict(in_dim=100, width=300, depth=3, seed=13, **kw), sd,
+                          x.numpy())
+    from silogic_b200.bitpacking.plan import HardPlan
+    plan = HardPlan.from_model(m.to(dev))
+    assert plan.chain() is not None
+    plan.chain_min_batch = 0
+    got = plan.counts(x.cuda()).cpu().numpy()
+    np.testing.assert_array_equal(got, ref)
+    plan.use_chain = False
+    np.testing.assert_array_equal(plan.counts(x.cuda()).cpu().numpy(), ref)
+
+
+def test_fc_chain_large_group_and_unsupported_plans():
+    """Wide last layer (group of 1300 rows per class) and the plans the chain declines."""
+    m = _rand_fc(50, 2600, 2, 17, node="walsh", connectome="topk", k=8, tau=10.0)
+    from silogic_b200.bitpacking.plan import HardPlan
+    plan = HardPlan.from_model(m.to(dev))
+    x = (torch.rand(777, 50, generator=torch.Generator().manual_seed(3)) < 0.5).to(torch.uint8)
+    plan.chain_min_batch = 0
+    a = plan.counts(x.cuda()).cpu().numpy()
+    plan.use_chain = False
+    np.testing.assert_array_equal(a, plan.counts(x.cuda()).cpu().numpy())
+    m3 = _rand_fc(50, 120, 2, 5, node="walsh", arity=3, connectome="fixed", tau=10.0)
+    assert HardPlan.from_model(m3.to(dev)).chain() is None
