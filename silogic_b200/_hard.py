@@ -140,6 +140,7 @@ def groupsum(x, B, num_classes, out=None):
 CHAIN_MAX_LAYERS = 32
 CHAIN_MAX_WIDTH = 13824
 CHAIN_MAX_CLASSES = 64
+CHAIN_MAX_SMEM = 227 * 1024           # opt-in shared memory per CTA on sm_100
 
 
 def chain_encode(idx, tt, wire_r=0):
@@ -281,6 +282,9 @@ class FCChain:
         self.in_dim, self.num_classes = int(in_dim), int(num_classes)
         self._w = (ctypes.c_int32 * len(self.widths))(*self.widths)
         self._off = (ctypes.c_int32 * len(self.class_off))(*self.class_off)
+        # one CTA per SM holds two layers of the column in shared memory
+        self.smem_bytes = 2 * max([self.in_dim] + self.widths) * 8
+        self.fits = self.smem_bytes <= CHAIN_MAX_SMEM
 
     @staticmethod
     def supported(steps, in_dim, num_classes):

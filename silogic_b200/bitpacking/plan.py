@@ -34,6 +34,8 @@ class HardPlan:
         if self._chain is None:
             self._chain = _hard.FCChain(self.steps, self.in_shape[1], self.num_classes,
                                         self.steps[0]["tt"].device)
+            if not self._chain.fits:
+                self._chain_ok, self._chain = False, None
         return self._chain
 
     # ----------------------------------------------------------- building
