@@ -42,6 +42,15 @@ sys.path.insert(0, ROOT)
 FIVE = [1 / 6, 2 / 6, 3 / 6, 4 / 6, 5 / 6]
 THIRTY_ONE = [(i + 1) / 32 for i in range(31)]
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant
+# kernel, averaged over the launches of one step, from one ncu capture of the same
+# command (the summaries under profiles/ name the command and list the figures).
+NCU_TRAFFIC = {
+    ("c2", "fc_chain"): (6.73e6, "profiles/fc_chain_c2_b65536.md"),
+    ("c3", "conv_hard"): ((7.894e6 + 16.335e6 + 8.051e6) / 3, "profiles/conv_hard_c3_b4096.md"),
+    ("c4", "conv_hard"): ((9.517e6 + 33.738e6) / 2, "profiles/conv_hard_c4_b8192.md"),
+}
+
 CONFIGS = {
     "c1": dict(ctor="LogicNet", inp="bern",
                kwargs=dict(in_dim=784, width=8000, depth=4, node="gate16", connectome="fixed",
@@ -564,7 +573,9 @@ def main():
             "gpu_launches": int(round(r["launches_per_step"] * a.steps)),
             "roofline": {"kernel": f"slg_{dom} ({dom_n:.0f} launches/step)", "bound": "hbm",
                          "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
-                         "peak_kind": kind, "traffic": None,
+                         "peak_kind": kind,
+                         "traffic": NCU_TRAFFIC.get((a.config, dom), (None,))[0] if not a.batch else None,
+                         "traffic_source": NCU_TRAFFIC.get((a.config, dom), (None, None))[1],
                          "algorithmic_bytes_per_step": dom_bytes,
                          "step_frac": r["bytes_per_sample"] * B / (ms_step * 1e-3) / 1e9 / hbm},
             "kernels_ms_per_step": {k: v[0] for k, v in r["kern"].items()},
