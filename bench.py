@@ -154,12 +154,22 @@ class ClockSampler:
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(self.rows)}
 
 
+_SYNC = None
+
+
 def flush_l2(buf):
     """Evict the step's data from L2 before a timed step: write a buffer larger than L2,
     then read it back, so L2 ends up holding clean lines of the flush buffer and the
     step does not pay for writing back the flush's own dirty lines."""
     buf.fill_(1)
     buf.sum()
+    # With several ranks, line their streams up after the flush (a one-element
+    # all-reduce, untimed) so a step's time does not include another rank's flush.
+    if torch.distributed.is_initialized() and torch.distributed.get_world_size() > 1:
+        global _SYNC
+        if _SYNC is None or _SYNC.device != buf.device:
+            _SYNC = torch.zeros(1, device=buf.device)
+        torch.distributed.all_reduce(_SYNC)
 
 
 def soak_until_sampled(step, clk, min_s=1.0, min_samples=4):
