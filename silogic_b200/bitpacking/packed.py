@@ -132,8 +132,9 @@ class BitpackedNet:
         self._graphs = {}
         self.device = _plan_device(plan)
 
-    def _graph_for(self, x, thresholds=None, mode=0):
-        """Cached :class:`HardGraph` for this input shape/dtype (and thresholds)."""
+    def _graph_for(self, x, thresholds=None, mode=0, slot=0):
+        """Cached :class:`HardGraph` for this input shape/dtype (and thresholds);
+        ``slot`` tells apart the double-buffered graphs of the pipelined path."""
         if isinstance(thresholds, (list, tuple)):
             tkey = tuple(float(v) for v in thresholds)
         elif thresholds is not None:
@@ -142,10 +143,11 @@ class BitpackedNet:
             tkey = (thresholds.data_ptr(), tuple(thresholds.shape))
         else:
             tkey = None
-        key = (tuple(x.shape), x.dtype, mode, tkey)
+        key = (tuple(x.shape), x.dtype, mode, tkey, slot)
         g = self._graphs.get(key)
         if g is None:
             if len(self._graphs) >= self.max_graphs:
+                torch.cuda.synchronize(self.device)     # no replay of it still pending
                 self._graphs.pop(next(iter(self._graphs)))
             static = torch.empty(x.shape, dtype=x.dtype, device=self.device)
             static.copy_(x)
@@ -153,12 +155,53 @@ class BitpackedNet:
             self._graphs[key] = g
         return g
 
+    def _run_pipelined(self, t, thresholds, mode):
+        """A large host batch in slices of ~``pipeline_bytes``: the host-to-device copy of
+        slice i+1 (side stream) overlaps the graph replay of slice i, alternating two
+        graphs with their own static inputs."""
+        B, sb = t.shape[0], self._slice(t)
+        dev = self.device
+        main = torch.cuda.current_stream(dev)
+        if getattr(self, "_copy_stream", None) is None:
+            self._copy_stream = torch.cuda.Stream(dev)
+        cs = self._copy_stream
+        logits = torch.empty((B, self.plan.num_classes), dtype=torch.float32, device=dev)
+        freed = [None, None]          # replay k no longer reads its static input
+        cs.wait_stream(main)
+        for i, s0 in enumerate(range(0, B, sb)):
+            part = t[s0:s0 + sb]
+            k = i % 2 if part.shape[0] == sb else 2
+            g = self._graph_for(part, thresholds, mode, slot=k)
+            with torch.cuda.stream(cs):
+                if k < 2 and freed[k] is not None:
+                    cs.wait_event(freed[k])
+                g.x.copy_(part, non_blocking=True)
+                copied = torch.cuda.Event()
+                copied.record(cs)
+            main.wait_event(copied)
+            g.graph.replay()
+            logits[s0:s0 + part.shape[0]].copy_(g.logits)
+            if k < 2:
+                freed[k] = torch.cuda.Event()
+                freed[k].record(main)
+        return logits
+
+    #: host batches are pipelined (see _run_pipelined) in slices of about this many
+    #: input bytes (a multiple of 1024 samples), when there are at least two slices
+    pipeline_bytes = 8 << 20
+
+    def _slice(self, t):
+        per = max(1, t[:1].numel() * t.element_size())
+        return max(1024, -(-(self.pipeline_bytes // per) // 1024) * 1024)
+
     def _run(self, x, thresholds=None, mode=0):
         """Logits of a numpy / host / device batch; host tensors are copied straight
         into the graph's static input (pinned memory makes that asynchronous)."""
         was_np = isinstance(x, np.ndarray)
         t = torch.from_numpy(np.ascontiguousarray(x)) if was_np else x
-        if self.graphs and t.shape[0] > 0:
+        if self.graphs and not t.is_cuda and t.shape[0] >= 2 * self._slice(t):
+            logits = self._run_pipelined(t, thresholds, mode)
+        elif self.graphs and t.shape[0] > 0:
             g = self._graph_for(t, thresholds, mode)
             g(t)
             logits = g.logits.clone()

@@ -292,3 +292,18 @@ def test_fc_chain_large_group_and_unsupported_plans():
     np.testing.assert_array_equal(a, plan.counts(x.cuda()).cpu().numpy())
     m3 = _rand_fc(50, 120, 2, 5, node="walsh", arity=3, connectome="fixed", tau=10.0)
     assert HardPlan.from_model(m3.to(dev)).chain() is None
+
+
+def test_pipelined_host_batches_match_one_shot():
+    """Host batches split into double-buffered, copy-overlapped slices give the same
+    logits as one graph over the whole batch (ragged last slice included)."""
+    from silogic_b200.bitpacking import convert_logic_net
+    m = _rand_fc(100, 300, 3, 21, node="walsh", connectome="topk", k=8, tau=10.0)
+    bp = convert_logic_net(m.to(dev))
+    x = (torch.rand(5000, 100, generator=torch.Generator().manual_seed(9)) < 0.3).to(torch.uint8)
+    ref = bp(x.cuda()).cpu().numpy()
+    bp.pipeline_bytes = 100 * 1024            # 1024-sample slices of 100 features
+    for xin in (x.pin_memory(), x, x.numpy()):
+        got = bp(xin)
+        got = got if isinstance(got, np.ndarray) else got.cpu().numpy()
+        np.testing.assert_array_equal(got, ref)
