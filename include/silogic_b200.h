@@ -199,7 +199,8 @@ int slg_fc_soft_bwd_noalloc(const float* x, int64_t in_dim, int64_t ldb, const i
  * conn_ste, or conn == NULL with K = 1 for fixed leaves); an arity-ary tree of `depth`
  * levels of `node` nodes (params [n, total_nodes, P] raw, level 0 first) combines the
  * leaves; channels n < wire_r copy input channel n; pool 2 takes the 2x2 max
- * (OR-pool) in the epilogue.  y is [n_out, Ho/pool, Wo/pool, ldb].
+ * (OR-pool) in the epilogue.  y is [n_out, Ho/pool, Wo/pool, ldb]; pool_arg (may be
+ * NULL) receives each pooled output's window argmax (uint8, same shape) for the backward.
  * Replaces tree_conv / tree_conv_topk / conv_hybrid (silogic/kernels/conv.py:354-400,
  * conv_topk.py:139-189, conv_hybrid.py:161-213), the PyTorch path of
  * ConvLogicTree.forward (silogic/layers.py:448-485) and OrPool.forward
@@ -208,7 +209,8 @@ int slg_conv_soft_fwd(const float* x, int64_t cin, int64_t H, int64_t W, int64_t
                       const int32_t* cand, const float* conn, int32_t K, int32_t conn_ste,
                       int32_t node, int32_t arity, int32_t depth, const float* params,
                       int32_t gate_hard, float inv_tau, int32_t kernel, int32_t pad,
-                      int64_t n_out, int64_t wire_r, int32_t pool, float* y, void* stream);
+                      int64_t n_out, int64_t wire_r, int32_t pool, float* y, uint8_t* pool_arg,
+                      void* stream);
 
 /* Bytes of scratch slg_conv_soft_bwd needs (per-CTA parameter-gradient partials). */
 int64_t slg_conv_soft_workspace_bytes(int64_t H, int64_t W, int64_t ldb, int32_t K, int32_t node,
@@ -218,15 +220,17 @@ int64_t slg_conv_soft_workspace_bytes(int64_t H, int64_t W, int64_t ldb, int32_t
 /* Backward of slg_conv_soft_fwd given gy [n_out, Ho/pool, Wo/pool, ldb]: routes each
  * pooled gradient to the first maximum of its window, back-propagates through the
  * tree, accumulates gx (caller zero-fills; NULL = skip) and writes gconn / gparams.
+ * pool_arg: the [n_out*Hp*Wp, ldb] uint8 window argmax the forward wrote (its
+ * pool_arg output, NULL there = not written); NULL here = re-evaluate every window.
  * Replaces TreeConvFn / TreeConvTopkFn / ConvHybridFn.backward (conv.py:379-396,
  * conv_topk.py:156-172, conv_hybrid.py:179-193). */
 int slg_conv_soft_bwd(const float* x, int64_t cin, int64_t H, int64_t W, int64_t ldb,
                       const int32_t* cand, const float* conn, int32_t K, int32_t conn_ste,
                       int32_t node, int32_t arity, int32_t depth, const float* params,
                       int32_t gate_hard, float inv_tau, int32_t kernel, int32_t pad,
-                      int64_t n_out, int64_t wire_r, int32_t pool, const float* gy, float* gx,
-                      float* gconn, float* gparams, void* workspace, int64_t workspace_bytes,
-                      void* stream);
+                      int64_t n_out, int64_t wire_r, int32_t pool, const float* gy,
+                      const uint8_t* pool_arg, float* gx, float* gconn, float* gparams,
+                      void* workspace, int64_t workspace_bytes, void* stream);
 
 /* -------------------------------------------------- soft-path boundaries */
 

@@ -44,9 +44,10 @@ _SIGS = {
     "slg_thermo_soft_fwd": [_p, _p, _i64, _i64, _i32, _p, _p],
     "slg_thermo_soft_bwd": [_p, _p, _p, _i64, _i64, _i32, _f32, _p, _p, _p],
     "slg_conv_soft_fwd": [_p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _i32, _p,
-                          _i32, _f32, _i32, _i32, _i64, _i64, _i32, _p, _p],
+                          _i32, _f32, _i32, _i32, _i64, _i64, _i32, _p, _p, _p],
     "slg_conv_soft_bwd": [_p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _i32, _p,
-                          _i32, _f32, _i32, _i32, _i64, _i64, _i32, _p, _p, _p, _p, _p, _i64, _p],
+                          _i32, _f32, _i32, _i32, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _i64,
+                          _p],
 }
 # entry points that do not return a status
 _RESTYPES = {

@@ -265,6 +265,11 @@ def _conv_meta(conv, wire_r=0, pool=1):
     return meta, params, conn
 
 
+#: keep the OR-pool window argmax from the conv forward for the backward (False: the
+#: backward re-evaluates every window; same results, more work)
+SAVE_POOL_ARGMAX = True
+
+
 class ConvSoft(torch.autograd.Function):
     """Feature-major conv tree block (+ OR-pool): xt [C*H*W, ldb] -> [n*Hp*Wp, ldb]."""
 
@@ -280,17 +285,22 @@ class ConvSoft(torch.autograd.Function):
         Wo = W + 2 * meta["pad"] - meta["kernel"] + 1
         Hp, Wp = Ho // meta["pool"], Wo // meta["pool"]
         y = torch.empty((meta["n_out"] * Hp * Wp, ldb), dtype=torch.float32, device=xt.device)
+        # keep each pooled output's window argmax for the backward (1 byte per output)
+        # instead of re-evaluating all the window's trees there
+        arg = None
+        if SAVE_POOL_ARGMAX and meta["pool"] > 1 and any(ctx.needs_input_grad[:3]):
+            arg = torch.empty((meta["n_out"] * Hp * Wp, ldb), dtype=torch.uint8, device=xt.device)
         call("slg_conv_soft_fwd", ptr(xt), C, H, W, ldb, ptr(meta["cand"]), ptr(connc), meta["K"],
              meta["ste"], meta["node"], meta["arity"], meta["depth"], ptr(params), meta["gate_hard"],
              meta["inv_tau"], meta["kernel"], meta["pad"], meta["n_out"], meta["wire_r"],
-             meta["pool"], ptr(y), stream_ptr(xt.device))
-        ctx.save_for_backward(xt, params, connc)
+             meta["pool"], ptr(y), ptr(arg), stream_ptr(xt.device))
+        ctx.save_for_backward(xt, params, connc, arg)
         ctx.meta, ctx.shape = meta, shape
         return y
 
     @staticmethod
     def backward(ctx, gy):
-        xt, params, connc = ctx.saved_tensors
+        xt, params, connc, arg = ctx.saved_tensors
         m = ctx.meta
         C, H, W = ctx.shape
         ldb = xt.shape[-1]
@@ -304,8 +314,8 @@ class ConvSoft(torch.autograd.Function):
         ws = torch.empty(max(nbytes, 4) // 4 + 1, dtype=torch.float32, device=xt.device)
         call("slg_conv_soft_bwd", ptr(xt), C, H, W, ldb, ptr(m["cand"]), ptr(connc), m["K"], m["ste"],
              m["node"], m["arity"], m["depth"], ptr(params), m["gate_hard"], m["inv_tau"],
-             m["kernel"], m["pad"], m["n_out"], m["wire_r"], m["pool"], ptr(gy), ptr(gx), ptr(gconn),
-             ptr(gparams), ptr(ws), ws.numel() * 4, stream_ptr(xt.device))
+             m["kernel"], m["pad"], m["n_out"], m["wire_r"], m["pool"], ptr(gy), ptr(arg), ptr(gx),
+             ptr(gconn), ptr(gparams), ptr(ws), ws.numel() * 4, stream_ptr(xt.device))
         return gx, gparams, gconn, None, None
 
 

@@ -42,9 +42,10 @@ extern "C" int slg_conv_soft_fwd(const float* x, int64_t cin, int64_t H, int64_t
                                  const int32_t* cand, const float* conn, int32_t K, int32_t conn_ste,
                                  int32_t node, int32_t arity, int32_t depth, const float* params,
                                  int32_t gate_hard, float inv_tau, int32_t kernel, int32_t pad,
-                                 int64_t n_out, int64_t wire_r, int32_t pool, float* y, void* stream) {
+                                 int64_t n_out, int64_t wire_r, int32_t pool, float* y,
+                                 uint8_t* pool_arg, void* stream) {
     ConvArgs A{x, cin, 0, 0, ldb, cand, conn, K, conn_ste, params, gate_hard, inv_tau,
-               kernel, pad, n_out, wire_r, pool, 0, 0};
+               kernel, pad, n_out, wire_r, pool, 0, 0, pool_arg};
     int st = conv_check(A, cin, H, W, "slg_conv_soft_fwd");
     if (st) return st;
     if (!y) return set_error(SLG_ERR_ARG, "slg_conv_soft_fwd: null output");
@@ -76,10 +77,10 @@ extern "C" int slg_conv_soft_bwd(const float* x, int64_t cin, int64_t H, int64_t
                                  int32_t node, int32_t arity, int32_t depth, const float* params,
                                  int32_t gate_hard, float inv_tau, int32_t kernel, int32_t pad,
                                  int64_t n_out, int64_t wire_r, int32_t pool, const float* gy,
-                                 float* gx, float* gconn, float* gparams, void* workspace,
-                                 int64_t workspace_bytes, void* stream) {
+                                 const uint8_t* pool_arg, float* gx, float* gconn, float* gparams,
+                                 void* workspace, int64_t workspace_bytes, void* stream) {
     ConvArgs A{x, cin, 0, 0, ldb, cand, conn, K, conn_ste, params, gate_hard, inv_tau,
-               kernel, pad, n_out, wire_r, pool, 0, 0};
+               kernel, pad, n_out, wire_r, pool, 0, 0, const_cast<uint8_t*>(pool_arg)};
     int st = conv_check(A, cin, H, W, "slg_conv_soft_bwd");
     if (st) return st;
     if (!gy || !gparams || !workspace) return set_error(SLG_ERR_ARG, "slg_conv_soft_bwd: null pointer");

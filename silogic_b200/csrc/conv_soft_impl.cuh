@@ -57,6 +57,10 @@ struct ConvArgs {
     const int32_t* cand; const float* conn; int K; int conn_ste;
     const float* params; int gate_hard; float inv_tau;
     int kernel; int pad; int64_t n_out; int64_t wire_r; int pool; int Hp; int Wp;
+    // pool window argmax per pooled output [n_out*Hp*Wp, ldb] (uint8, window index in
+    // row-major order): written by the forward when non-null, read by the backward
+    // instead of re-evaluating the window's trees
+    uint8_t* pool_arg;
 };
 
 // stage the channel's taps, weights and node parameters (whole block)
@@ -178,13 +182,15 @@ conv_soft_fwd_kernel(ConvArgs A, float* __restrict__ y) {
         const int64_t b = b0 + it * 32 + lane;
         if (b >= A.ldb) break;
         float best = 0.f;
+        int bq = 0;
         for (int q = 0; q < A.pool * A.pool; ++q) {
             const int yy = py * A.pool + q / A.pool, xx = px * A.pool + q % A.pool;
             const float v = wired ? __ldg(&A.x[((n * A.H + yy) * (int64_t)A.W + xx) * A.ldb + b])
                                   : conv_tree_value<NODE, AR, D, KT>(S, A, pos + q * L * KT, b, vals);
-            if (q == 0 || v > best) best = v;
+            if (q == 0 || v > best) { best = v; bq = q; }
         }
         y[((n * npos) + p) * A.ldb + b] = best;
+        if (A.pool_arg) A.pool_arg[((n * npos) + p) * A.ldb + b] = (uint8_t)bq;
     }
 }
 
@@ -249,9 +255,12 @@ conv_soft_bwd_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict
             const int64_t b = b0 + it * 32 + lane;
             if (b >= A.ldb) break;
             const float g = gy[((n * npos) + p) * A.ldb + b];
-            // argmax position of the pool window (first maximum)
+            // argmax position of the pool window (first maximum): saved by the forward,
+            // else recomputed
             int bq = 0;
-            if (A.pool > 1) {
+            if (A.pool > 1 && A.pool_arg) {
+                bq = A.pool_arg[((n * npos) + p) * A.ldb + b];
+            } else if (A.pool > 1) {
                 float best = 0.f;
                 for (int q = 0; q < A.pool * A.pool; ++q) {
                     const float v = conv_tree_value<NODE, AR, D, KT>(S, A, pos + q * L * KT, b, vals);

@@ -279,3 +279,27 @@ def test_conv_layer_soft_unpooled_vs_oracle():
     ref = OS.conv_block(Bk, P, x, training=True)
     got = conv.to(dev)(x.to(dev))
     np.testing.assert_allclose(got.detach().cpu().numpy(), ref.detach().numpy(), rtol=1e-5, atol=1e-6)
+
+
+def test_conv_backward_with_saved_pool_argmax_matches_recompute():
+    """The backward that reads the forward's saved window argmax gives the gradients of
+    the one that re-evaluates every window (gx within atomic-order rounding)."""
+    import silogic_b200._soft as SS
+    kw = dict(in_channels=15, in_hw=16, channels=[32, 64], head_widths=[320], tree_depth=2,
+              node="gate16", tau=20.0, seed=0)
+    m = _rand_model("LogicConvNet", kw, 31).to(dev).train()
+    g = torch.Generator().manual_seed(5)
+    x = (torch.rand(200, 15, 16, 16, generator=g) < 0.5).float().to(dev)
+    rmat = torch.randn(200, 10, generator=g).to(dev)
+    grads = []
+    for save in (True, False):
+        SS.SAVE_POOL_ARGMAX = save
+        try:
+            m.zero_grad()
+            xd = x.clone().requires_grad_(True)
+            (m(xd) * rmat).sum().backward()
+            grads.append([xd.grad.clone()] + [p.grad.clone() for p in m.parameters()])
+        finally:
+            SS.SAVE_POOL_ARGMAX = True
+    for a, b in zip(*grads):
+        torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)
