@@ -27,6 +27,8 @@ static int conv_check(ConvArgs& A, int64_t cin, int64_t H, int64_t W, const char
     if (A.wire_r > 0 && (A.wire_r > cin || A.wire_r > A.n_out || Ho > H || Wo > W))
         return set_error(SLG_ERR_ARG, "%s: wire_r needs cin >= wire_r and a same-size output", name);
     if (!A.x || !A.cand || !A.params) return set_error(SLG_ERR_ARG, "%s: null pointer", name);
+    if ((A.ldb & 3) || !aligned16(A.x) || (reinterpret_cast<uintptr_t>(A.pool_arg) & 3))
+        return set_error(SLG_ERR_ALIGN, "%s: ldb must be a multiple of 4, x 16-byte aligned", name);
     if (cdiv(A.ldb, 32 * CS_ITER) > 65535) return set_error(SLG_ERR_ARG, "%s: batch too large", name);
     A.C = cin; A.H = (int)H; A.W = (int)W;
     A.Hp = (int)(Ho / A.pool); A.Wp = (int)(Wo / A.pool);
@@ -49,6 +51,7 @@ extern "C" int slg_conv_soft_fwd(const float* x, int64_t cin, int64_t H, int64_t
     int st = conv_check(A, cin, H, W, "slg_conv_soft_fwd");
     if (st) return st;
     if (!y) return set_error(SLG_ERR_ARG, "slg_conv_soft_fwd: null output");
+    if (!aligned16(y)) return set_error(SLG_ERR_ALIGN, "slg_conv_soft_fwd: y not 16-byte aligned");
     if (n_out == 0 || A.Hp == 0 || A.Wp == 0) return SLG_OK;
     if (!conv_dispatch(node, arity, depth, false, A, y, nullptr, nullptr, nullptr, nullptr, nullptr,
                        as_stream(stream)))

@@ -159,6 +159,53 @@ __device__ __forceinline__ float conv_tree_value(const ConvSmem<NODE, AR, D>& S,
     return vals[in_base];
 }
 
+// Same tree on 4 consecutive samples b4..b4+3 (one float4 per tap read): the tap
+// position / weight reads and the address arithmetic are shared by the 4 samples.
+template <int NODE, int AR, int D, int KT>
+__device__ __forceinline__ float4 conv_tree_value4(const ConvSmem<NODE, AR, D>& S, const ConvArgs& A,
+                                                   const int* __restrict__ posq, int64_t b4) {
+    constexpr int L = TreeShape<AR, D>::L;
+    constexpr int NPS = NodeStage<NODE, AR>::NPS;
+    const int K = A.K;
+    float vals[4][2 * L];
+#pragma unroll
+    for (int l = 0; l < L; ++l) {
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < KT; ++k) {
+            if (k < K && S.w[l * K + k] != 0.0f) {
+                const int p = posq[l * K + k];
+                if (p >= 0) {
+                    const float w = S.w[l * K + k];
+                    const float4 v = __ldg(reinterpret_cast<const float4*>(A.x + (int64_t)p * A.ldb + b4));
+                    s.x += w * v.x; s.y += w * v.y; s.z += w * v.z; s.w += w * v.w;
+                }
+            }
+        }
+        vals[0][l] = s.x; vals[1][l] = s.y; vals[2][l] = s.z; vals[3][l] = s.w;
+    }
+    int in_base = 0, out_base = L, width = L, node_base = 0;
+#pragma unroll
+    for (int lev = 0; lev < D; ++lev) {
+        const int nn = width / AR;
+#pragma unroll
+        for (int m = 0; m < nn; ++m) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                float a[AR];
+#pragma unroll
+                for (int j = 0; j < AR; ++j) a[j] = vals[e][in_base + m * AR + j];
+                vals[e][out_base + m] = node_fwd<NODE, AR>(S.np + (node_base + m) * NPS, a);
+            }
+        }
+        in_base = out_base;
+        out_base += nn;
+        node_base += nn;
+        width = nn;
+    }
+    return make_float4(vals[0][in_base], vals[1][in_base], vals[2][in_base], vals[3][in_base]);
+}
+
 template <int NODE, int AR, int D, int KT>
 __global__ void __launch_bounds__(CS_WARPS * 32)
 conv_soft_fwd_kernel(ConvArgs A, float* __restrict__ y) {
@@ -176,21 +223,25 @@ conv_soft_fwd_kernel(ConvArgs A, float* __restrict__ y) {
     const int py = p / A.Wp, px = p % A.Wp;
     int* pos = s_pos[threadIdx.x >> 5];
     if (!wired) conv_fill_pos<NODE, AR, D, KT>(S, A, py, px, pos, lane);
+    // lane = 4 consecutive samples (ldb is a multiple of 4): float4 tap reads
     const int64_t b0 = (int64_t)blockIdx.y * (32 * CS_ITER);
-    float vals[2 * L];
-    for (int it = 0; it < CS_ITER; ++it) {
-        const int64_t b = b0 + it * 32 + lane;
+    for (int it = 0; it < CS_ITER / 4; ++it) {
+        const int64_t b = b0 + (it * 32 + lane) * 4;
         if (b >= A.ldb) break;
-        float best = 0.f;
-        int bq = 0;
+        float4 best = make_float4(0.f, 0.f, 0.f, 0.f);
+        uchar4 bq = make_uchar4(0, 0, 0, 0);
         for (int q = 0; q < A.pool * A.pool; ++q) {
             const int yy = py * A.pool + q / A.pool, xx = px * A.pool + q % A.pool;
-            const float v = wired ? __ldg(&A.x[((n * A.H + yy) * (int64_t)A.W + xx) * A.ldb + b])
-                                  : conv_tree_value<NODE, AR, D, KT>(S, A, pos + q * L * KT, b, vals);
-            if (q == 0 || v > best) { best = v; bq = q; }
+            const float4 v = wired
+                ? __ldg(reinterpret_cast<const float4*>(A.x + ((n * A.H + yy) * (int64_t)A.W + xx) * A.ldb + b))
+                : conv_tree_value4<NODE, AR, D, KT>(S, A, pos + q * L * KT, b);
+            if (q == 0 || v.x > best.x) { best.x = v.x; bq.x = (uint8_t)q; }
+            if (q == 0 || v.y > best.y) { best.y = v.y; bq.y = (uint8_t)q; }
+            if (q == 0 || v.z > best.z) { best.z = v.z; bq.z = (uint8_t)q; }
+            if (q == 0 || v.w > best.w) { best.w = v.w; bq.w = (uint8_t)q; }
         }
-        y[((n * npos) + p) * A.ldb + b] = best;
-        if (A.pool_arg) A.pool_arg[((n * npos) + p) * A.ldb + b] = (uint8_t)bq;
+        *reinterpret_cast<float4*>(y + ((n * npos) + p) * A.ldb + b) = best;
+        if (A.pool_arg) *reinterpret_cast<uchar4*>(A.pool_arg + ((n * npos) + p) * A.ldb + b) = bq;
     }
 }
 
