@@ -307,3 +307,17 @@ def test_pipelined_host_batches_match_one_shot():
         got = bp(xin)
         got = got if isinstance(got, np.ndarray) else got.cpu().numpy()
         np.testing.assert_array_equal(got, ref)
+
+
+def test_chain_encode_records_on_device():
+    """slg_fc_chain_encode packs (in_a, in_b, table) records, residual wires included."""
+    from silogic_b200 import _hard
+    g = torch.Generator().manual_seed(4)
+    idx = torch.randint(0, 9000, (5000, 2), generator=g, dtype=torch.int32)
+    tt = torch.randint(0, 16, (5000,), generator=g, dtype=torch.int64)
+    rec = _hard.chain_encode(idx.cuda(), tt.cuda(), wire_r=100).cpu().numpy().view(np.uint32)
+    i, t = idx.numpy().astype(np.uint32), tt.numpy().astype(np.uint32)
+    ref = i[:, 0] | (i[:, 1] << 14) | (t << 28)
+    o = np.arange(100, dtype=np.uint32)
+    ref[:100] = o | (o << 14) | np.uint32(0xA << 28)
+    np.testing.assert_array_equal(rec, ref)
