@@ -14,8 +14,9 @@ class HardPlan:
     """Wiring + truth tables of every layer, on the parameters' device."""
 
     #: batches at least this large run an all-FC arity-2 plan as one persistent
-    #: kernel (``_hard.FCChain``: activations stay in shared memory between layers)
-    chain_min_batch = 8192
+    #: kernel (``_hard.FCChain``: activations stay in shared memory between layers);
+    #: measured faster than the per-layer kernels from 1,024 samples up
+    chain_min_batch = 0
 
     def __init__(self, steps, in_shape, num_classes, tau):
         self.steps = steps            # list of dicts, see from_model
