@@ -120,10 +120,12 @@ __device__ __forceinline__ void conv_fill_pos(const ConvSmem<NODE, AR, D>& S, co
     __syncwarp();
 }
 
+// tap values kept by the backward for its connection gradients (none: pass nullptr)
 template <int NODE, int AR, int D, int KT>
 __device__ __forceinline__ float conv_tree_value(const ConvSmem<NODE, AR, D>& S, const ConvArgs& A,
                                                  const int* __restrict__ posq, int64_t b,
-                                                 float (&vals)[2 * TreeShape<AR, D>::L]) {
+                                                 float (&vals)[2 * TreeShape<AR, D>::L],
+                                                 float* taps = nullptr) {
     constexpr int L = TreeShape<AR, D>::L;
     constexpr int NPS = NodeStage<NODE, AR>::NPS;
     const int K = A.K;
@@ -132,10 +134,16 @@ __device__ __forceinline__ float conv_tree_value(const ConvSmem<NODE, AR, D>& S,
         float s = 0.f;
 #pragma unroll
         for (int k = 0; k < KT; ++k) {
-            // zero weights (one-hot straight-through selection) contribute nothing: skip the load
-            if (k < K && S.w[l * K + k] != 0.0f) {
+            if (taps) taps[l * KT + k] = 0.f;
+            if (k < K) {
                 const int p = posq[l * K + k];
-                if (p >= 0) s += S.w[l * K + k] * __ldg(&A.x[(int64_t)p * A.ldb + b]);
+                // zero weights (one-hot straight-through selection) contribute nothing to the
+                // value: skip the load unless the backward wants the tap
+                if (p >= 0 && (taps || S.w[l * K + k] != 0.0f)) {
+                    const float v = __ldg(&A.x[(int64_t)p * A.ldb + b]);
+                    s += S.w[l * K + k] * v;
+                    if (taps) taps[l * KT + k] = v;
+                }
             }
         }
         vals[l] = s;
@@ -319,7 +327,10 @@ conv_soft_bwd_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict
                 }
             }
             const int* posq = pos + bq * L * KT;
-            conv_tree_value<NODE, AR, D, KT>(S, A, posq, b, vals);
+            // small trees keep their tap values in registers for the connection gradients
+            constexpr bool KEEP = L * KT <= 32;
+            float taps[KEEP ? L * KT : 1];
+            conv_tree_value<NODE, AR, D, KT>(S, A, posq, b, vals, KEEP ? taps : nullptr);
             // reverse pass through the tree: adjoints indexed like vals; level bases:
             // leaves at 0, level i (1..D) at L + sum_{j<i} L/AR^j
             float adj[2 * L];
@@ -358,7 +369,7 @@ conv_soft_bwd_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict
                         const int e = l * K + k;
                         if (posq[e] >= 0) {
                             const int64_t idx = (int64_t)posq[e] * A.ldb + b;
-                            acc_w[l * KT + k] += gl * __ldg(&A.x[idx]);
+                            acc_w[l * KT + k] += gl * (KEEP ? taps[l * KT + k] : __ldg(&A.x[idx]));
                             if (gx && S.w[e] != 0.0f) atomicAdd(&gx[idx], gl * S.w[e]);
                         }
                     }
