@@ -21,6 +21,9 @@ namespace slg {
 constexpr int CS_WARPS = 8;
 constexpr int CS_ITER = 8;          // samples per lane per chunk -> 256 samples / chunk
 constexpr int CS_KMAX = 16;
+#ifndef SLG_CS_BWD_MINB
+#define SLG_CS_BWD_MINB 2       // 2 CTAs per SM: wide-LUT backward trades a few spills for occupancy
+#endif
 
 template <int AR>
 __host__ __device__ constexpr int ipow_ar(int e) {
@@ -256,7 +259,7 @@ conv_soft_fwd_kernel(ConvArgs A, float* __restrict__ y) {
 // workspace rows: ws[(blockIdx.y * tiles + tile) * n_out + n][NPART],
 // NPART = L*K (conn) + NODES*NPG (node)
 template <int NODE, int AR, int D, int KT>
-__global__ void __launch_bounds__(CS_WARPS * 32)
+__global__ void __launch_bounds__(CS_WARPS * 32, SLG_CS_BWD_MINB)
 conv_soft_bwd_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict__ gx,
                      float* __restrict__ ws, int npart) {
     constexpr int L = TreeShape<AR, D>::L;
@@ -307,7 +310,6 @@ conv_soft_bwd_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict
         for (int q = 0; q < NPG; ++q) acc_n[m][q] = 0.f;
 
     if (p < npos) {
-        const int py = p / A.Wp, px = p % A.Wp;
         const int64_t b0 = (int64_t)blockIdx.y * (32 * CS_ITER);
         float vals[2 * L];
         for (int it = 0; it < CS_ITER; ++it) {

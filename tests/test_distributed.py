@@ -56,6 +56,20 @@ def _worker_gather(rank, ws, port, q):
         D.allreduce_gradients([p, r])
         ok = ok and torch.allclose(p.grad, torch.full((3, 4), 1.5)) and \
             torch.allclose(r.grad, torch.full((5,), 3.0))
+        # sharded_hard_counts: each rank runs only its shard (a stand-in plan whose
+        # counts are a function of the rows), and every rank gets the whole batch
+        seen = []
+
+        class _Plan:
+            num_classes = 3
+
+            def counts(self, xs):
+                seen.append(xs.shape[0])
+                return (xs[:, :3] * 2).to(torch.int32)
+        x = torch.arange(777 * 5, dtype=torch.int32).view(777, 5)
+        got = D.sharded_hard_counts(_Plan(), x)
+        a, b = D.shard_range(777, ws, rank)
+        ok = ok and torch.equal(got, (x[:, :3] * 2).to(torch.int32)) and seen == [b - a]
         q.put((rank, bool(ok)))
         dist.destroy_process_group()
     except Exception as e:   # report instead of hanging the parent
