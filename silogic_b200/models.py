@@ -60,6 +60,9 @@ class LogicNet(nn.Module):
     def forward_hard(self, x):
         from .bitpacking.plan import HardPlan
         plan = HardPlan.from_model(self)
+        # per-layer kernels: the fused FC stack's host-side layout planning (about a
+        # second for a 6 x 10,000 net) only pays off on a converted, reused BitpackedNet
+        plan.use_chain = False
         if isinstance(self.head, GroupSum):
             return plan.counts(x).float()
         return self.head.forward_hard(plan.features(x))
@@ -158,6 +161,9 @@ class LogicConvNet(nn.Module):
     def forward_hard(self, x):
         from .bitpacking.plan import HardPlan
         plan = HardPlan.from_model(self)
+        # per-layer kernels: the fused FC stack's host-side layout planning (about a
+        # second for a 6 x 10,000 net) only pays off on a converted, reused BitpackedNet
+        plan.use_chain = False
         if isinstance(self.head, GroupSum):
             return plan.counts(x).float()
         return self.head.forward_hard(plan.features(x))
