@@ -124,6 +124,18 @@ int slg_groupsum(const uint64_t* x, int64_t width, int64_t ldw, int64_t B,
 #define SLG_CHAIN_MAX_LAYERS 32
 #define SLG_CHAIN_MAX_WIDTH 13824
 #define SLG_CHAIN_MAX_CLASSES 64
+/* Host-side planner (no GPU work; all pointers are HOST memory) of a conflict-free
+ * record layout for slg_fc_chain_counts: each layer's nodes are ordered in half-warps
+ * whose 16 lanes read distinct shared-memory bank pairs (a bipartite edge colouring of
+ * the nodes' input bank pairs) and padded with nodes nothing reads; the last layer is
+ * laid out per class block with constant-zero padding rows.  idx = the layers'
+ * [out_dims[l], 2] wirings concatenated, tt = their tables (low 4 bits), wire_r[l]
+ * leading residual wires; reorder = 0 keeps natural order.  Writes rec (capacity
+ * rec_capacity records), widths[n_layers] and class_off[num_classes + 1]. */
+int slg_fc_chain_plan(int64_t in_dim, int32_t n_layers, const int64_t* out_dims,
+                      const int32_t* idx, const uint64_t* tt, const int64_t* wire_r,
+                      int32_t num_classes, int32_t reorder, uint32_t* rec, int64_t rec_capacity,
+                      int32_t* widths, int32_t* class_off);
 int slg_fc_chain_encode(const int32_t* idx, const uint64_t* tt, int64_t out_dim, int64_t wire_r,
                         uint32_t* rec, void* stream);
 int64_t slg_fc_chain_smem_bytes(int64_t in_dim, const int32_t* widths, int32_t n_layers);

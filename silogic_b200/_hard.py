@@ -153,124 +153,28 @@ def chain_encode(idx, tt, wire_r=0):
     return rec
 
 
-def _half_warps(ka, kb, nodes):
-    """Split ``nodes`` into half-warps (<= 16 lanes) whose 64-bit shared loads are free of
-    bank conflicts: within a half-warp every node's first input sits in a distinct
-    8-byte bank pair (``ka``) and so does its second (``kb``).  A half-warp is a
-    matching of the bipartite multigraph bank-pair(a) -- node -- bank-pair(b), so this
-    is a bipartite edge colouring; the alternating-path method (Konig) uses exactly
-    max-degree colours, the fewest possible."""
-    adj = {}                      # (side, bank) -> {colour: node}
-    colour = {}
-
-    def free(v):
-        d = adj.setdefault(v, {})
-        c = 0
-        while c in d:
-            c += 1
-        return c
-
-    for j in nodes:
-        u, v = ("a", ka[j]), ("b", kb[j])
-        du, dv = adj.setdefault(u, {}), adj.setdefault(v, {})
-        al, be = free(u), free(v)
-        if al not in dv:
-            pass
-        else:
-            # swap colours al/be along the alternating path that starts at v with al;
-            # in a bipartite graph it cannot end at u, so al becomes free at v
-            path, x, c = [], v, al
-            while c in adj[x]:
-                e = adj[x][c]
-                path.append(e)
-                y = ("b", kb[e]) if x == ("a", ka[e]) else ("a", ka[e])
-                x, c = y, (be if c == al else al)
-            for e in path:
-                ea, eb = ("a", ka[e]), ("b", kb[e])
-                del adj[ea][colour[e]]
-                del adj[eb][colour[e]]
-            for e in path:
-                colour[e] = be if colour[e] == al else al
-                adj[("a", ka[e])][colour[e]] = e
-                adj[("b", kb[e])][colour[e]] = e
-        colour[j] = al
-        du[al] = j
-        dv[al] = j
-    halves = {}
-    for j in nodes:
-        halves.setdefault(colour[j], []).append(j)
-    return [halves[c] for c in sorted(halves)]
-
-
 def chain_layout(steps, in_dim, num_classes, reorder=True):
-    """Node records, layer widths and class offsets for :class:`FCChain`.
-
-    Each layer's nodes are stored in the order they are processed (lanes of warp ``w``
-    of an iteration handle slots ``32w .. 32w+31``), arranged in half-warps whose
-    lanes read their two inputs from distinct shared-memory bank pairs (no bank
-    conflicts); half-warps are padded to 16 lanes with constant-zero nodes that read
-    a live lane's inputs (a broadcast).  The last layer is arranged per class block so
-    GroupSum reads class ``c`` as slots ``[off[c], off[c+1])`` (padding rows are zero).
-    A layer whose arrangement would exceed the width limit keeps its natural order.
-    Returns ``(records uint32 numpy, widths, class offsets)``; record =
-    in_a | in_b << 14 | table << 28 over storage slots.
-    """
+    """Node records, layer widths and class offsets for :class:`FCChain`, planned by the
+    library's host-side planner ``slg_fc_chain_plan`` (bank-conflict-free half-warps,
+    padded layers, per-class blocks in the last layer).  Returns ``(records uint32
+    numpy, widths, class offsets)``; record = in_a | in_b << 14 | table << 28 over
+    storage slots."""
     import numpy as np
-    pos = np.arange(in_dim)
-    recs, widths = [], []
-    class_off = None
-    for li, st in enumerate(steps):
-        idx = st["idx"].detach().cpu().numpy().astype(np.int64)
-        tt = st["tt"].detach().cpu().numpy().astype(np.int64)
-        out = idx.shape[0]
-        a, b, g = pos[idx[:, 0]], pos[idx[:, 1]], tt & 15
-        wr = int(st["wire_r"])
-        if wr:   # residual wire: identity on the first input (address a + 2b -> 0b1010)
-            a[:wr] = pos[:wr]
-            b[:wr] = pos[:wr]
-            g[:wr] = 0xA
-        node_rec = (a | (b << 14) | (g << 28)).astype(np.uint32)
-        ka, kb = (a % 16).tolist(), (b % 16).tolist()
-        last = li == len(steps) - 1
-        G = out // num_classes
-        blocks = [range(c * G, (c + 1) * G) for c in range(num_classes)] if last else [range(out)]
-        layout = None
-        if reorder:
-            layout = []
-            for blk in blocks:
-                hw = _half_warps(ka, kb, blk)
-                hw += [[]] * (len(hw) % 2)                    # whole warps per block
-                layout.append(hw)
-            if sum(len(h) for h in layout) * 16 > CHAIN_MAX_WIDTH:
-                layout = None
-        if layout is None:   # natural order, blocks padded to whole warps
-            layout = [[list(blk[i:i + 16]) for i in range(0, len(blk), 16)] for blk in blocks]
-            layout = [hw + [[]] * (len(hw) % 2) for hw in layout]
-        width = sum(len(h) for h in layout) * 16
-        slot = np.zeros(out, dtype=np.int64)
-        rec = np.zeros(width, dtype=np.uint32)
-        offs = [0]
-        s0 = 0
-        rot = 0
-        for hw in layout:
-            for half in hw:
-                # live lanes start at a rotating offset so padding does not pile up in
-                # the same bank pairs (which would skew the next layer's reads)
-                lanes = (rot + np.arange(16)) % 16
-                rot = (rot + 16 - len(half)) % 16
-                slot[half] = s0 + lanes[:len(half)]
-                if half and len(half) < 16:
-                    # padding lanes: a live lane's inputs (broadcast), constant-zero table
-                    rec[s0 + lanes[len(half):]] = node_rec[half[0]] & np.uint32(0x0fffffff)
-                s0 += 16
-            offs.append(s0)
-        rec[slot] = node_rec
-        recs.append(rec)
-        widths.append(width)
-        if last:
-            class_off = offs
-        pos = slot
-    return np.concatenate(recs), widths, class_off
+    outs = np.array([st["idx"].shape[0] for st in steps], dtype=np.int64)
+    idx = np.ascontiguousarray(np.concatenate(
+        [st["idx"].detach().cpu().numpy().astype(np.int32).reshape(-1) for st in steps]))
+    tt = np.ascontiguousarray(np.concatenate(
+        [st["tt"].detach().cpu().numpy().astype(np.int64).view(np.uint64) for st in steps]))
+    wr = np.array([int(st["wire_r"]) for st in steps], dtype=np.int64)
+    cap = len(steps) * CHAIN_MAX_WIDTH
+    rec = np.zeros(cap, dtype=np.uint32)
+    widths = np.zeros(len(steps), dtype=np.int32)
+    off = np.zeros(num_classes + 1, dtype=np.int32)
+    P = ctypes.c_void_p
+    call("slg_fc_chain_plan", int(in_dim), len(steps), P(outs.ctypes.data), P(idx.ctypes.data),
+         P(tt.ctypes.data), P(wr.ctypes.data), int(num_classes), int(bool(reorder)),
+         P(rec.ctypes.data), cap, P(widths.ctypes.data), P(off.ctypes.data))
+    return rec[:int(widths.sum())].copy(), widths.tolist(), off.tolist()
 
 
 class FCChain:

@@ -60,8 +60,8 @@ class LogicNet(nn.Module):
     def forward_hard(self, x):
         from .bitpacking.plan import HardPlan
         plan = HardPlan.from_model(self)
-        # per-layer kernels: the fused FC stack's host-side layout planning (about a
-        # second for a 6 x 10,000 net) only pays off on a converted, reused BitpackedNet
+        # per-layer kernels: the fused FC stack's host-side layout planning and record
+        # upload pay off on a converted, reused BitpackedNet, not on every call
         plan.use_chain = False
         if isinstance(self.head, GroupSum):
             return plan.counts(x).float()
@@ -161,8 +161,8 @@ class LogicConvNet(nn.Module):
     def forward_hard(self, x):
         from .bitpacking.plan import HardPlan
         plan = HardPlan.from_model(self)
-        # per-layer kernels: the fused FC stack's host-side layout planning (about a
-        # second for a 6 x 10,000 net) only pays off on a converted, reused BitpackedNet
+        # per-layer kernels: the fused FC stack's host-side layout planning and record
+        # upload pay off on a converted, reused BitpackedNet, not on every call
         plan.use_chain = False
         if isinstance(self.head, GroupSum):
             return plan.counts(x).float()
