@@ -144,6 +144,14 @@ int slg_fc_chain_counts(const uint64_t* x, int64_t in_dim, int64_t ldw, int64_t 
                         int32_t num_classes, const int32_t* class_off, int32_t* counts,
                         void* stream);
 
+/* Learned linear readout on packed features: out[b*C + c] = bias[c] (NULL = 0) +
+ * sum_f W[c*width + f] * bit f of sample b, fp32 (x [width, ldw], width <= 25,600).
+ * Replaces BitpackedLearnedHead.forward (silogic/bitpacking/packed_layer.py:574-605),
+ * which unpacks and multiplies on the host; summation order differs from a BLAS sgemm
+ * (fp32 rounding), integer-valued weights (ternary heads) give exact results. */
+int slg_packed_linear(const uint64_t* x, int64_t width, int64_t ldw, int64_t B, const float* W,
+                      const float* bias, int32_t num_classes, float* out, void* stream);
+
 /* ------------------------------------------------------- soft FC layer */
 
 /* Node kinds of the soft kernels. */

@@ -136,6 +136,18 @@ def groupsum(x, B, num_classes, out=None):
     return out
 
 
+def packed_linear(x, W, bias, B):
+    """Learned readout ``[B, C]`` fp32 = bits of packed ``x`` ``[width, ldw]`` @ ``W.T`` + bias."""
+    require_cuda(x)
+    W = W.float().contiguous()
+    bias = bias.float().contiguous() if bias is not None else None
+    width = x.numel() // x.shape[-1]
+    out = torch.empty((B, W.shape[0]), dtype=torch.float32, device=x.device)
+    call("slg_packed_linear", ptr(x), width, x.shape[-1], B, ptr(W), ptr(bias), W.shape[0], ptr(out),
+         stream_ptr(x.device))
+    return out
+
+
 # ------------------------------------------- whole FC stack in one launch
 CHAIN_MAX_LAYERS = 32
 CHAIN_MAX_WIDTH = 13824

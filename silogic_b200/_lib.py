@@ -29,6 +29,7 @@ _SIGS = {
     "slg_conv_hard": [_p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _i64, _i64,
                       _i32, _p, _p],
     "slg_groupsum": [_p, _i64, _i64, _i64, _i32, _p, _p],
+    "slg_packed_linear": [_p, _i64, _i64, _i64, _p, _p, _i32, _p, _p],
     "slg_fc_chain_encode": [_p, _p, _i64, _i64, _p, _p],
     "slg_fc_chain_plan": [_i64, _i32, _p, _p, _p, _p, _i32, _i32, _p, _i64, _p, _p],
     "slg_fc_chain_counts": [_p, _i64, _i64, _i64, _p, _p, _i32, _i32, _p, _p, _p],

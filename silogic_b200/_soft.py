@@ -65,7 +65,7 @@ class FromFeatureMajor(torch.autograd.Function):
 # --------------------------------------------------------------- FC layer
 def fc_supported(layer):
     from .connectomes import FixedConnectome, TopKConnectome
-    if layer.node.kind not in NODE_ID:
+    if layer.node.kind not in NODE_ID and layer.node.kind != "polynomial":
         return False
     if not isinstance(layer._conn, (FixedConnectome, TopKConnectome)):
         return False
@@ -99,6 +99,8 @@ def _fc_meta(layer, wire_r=0):
             params = (params + g) / node.gumbel_tau
             gate_hard = 1
     inv_tau = float(node.inv_tau) if kind == "walsh" else 1.0
+    if kind == "polynomial":    # same function in the Walsh basis (see PolynomialNode)
+        params, kind = node.walsh_theta(), "walsh"
     return dict(cand=cand.contiguous(), K=K, ste=ste, node=NODE_ID[kind], arity=layer.arity,
                 gate_hard=gate_hard, inv_tau=inv_tau, out_dim=layer.out_dim,
                 wire_r=wire_r), params, conn

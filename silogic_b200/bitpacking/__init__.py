@@ -10,7 +10,12 @@ from .. import _hard
 from .plan import HardPlan, HardGraph
 from .convert import convert_logic_net, convert_logic_conv_net, convert_layer, convert_head
 from .packed import (BitpackedNet, BitpackedConvNet, BitpackedConvGPUNet, BitpackedGPULayer,
-                     BitpackedConvGPULayer, packed_unfold_gpu, packed_or_pool_gpu)
+                     BitpackedConvGPULayer, packed_unfold_gpu, packed_or_pool_gpu,
+                     PackedGroupSumHead, PackedLearnedHead)
+
+# reference names of the bit-packed heads (packed_layer.py:545-605)
+BitpackedGroupSumHead = PackedGroupSumHead
+BitpackedLearnedHead = PackedLearnedHead
 
 # GPU bit-packed kernels are available (name kept from the reference; no Triton is used).
 HAS_TRITON = True
@@ -43,4 +48,5 @@ def unpack_bits(packed, B):
 __all__ = ["convert_logic_net", "convert_logic_conv_net", "convert_layer", "convert_head",
            "BitpackedNet", "BitpackedConvNet", "BitpackedConvGPUNet", "BitpackedGPULayer",
            "BitpackedConvGPULayer", "packed_unfold_gpu", "packed_or_pool_gpu",
-           "pack_bits", "unpack_bits", "n_words", "HAS_TRITON"]
+           "pack_bits", "unpack_bits", "n_words", "HAS_TRITON", "BitpackedGroupSumHead",
+           "BitpackedLearnedHead", "HardPlan", "HardGraph"]

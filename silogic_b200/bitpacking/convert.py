@@ -8,7 +8,7 @@ import torch
 
 from .. import _hard
 from ..connectomes import SumThresholdConnectome
-from .packed import (PackedFCLayer, PackedConvLayer, BitpackedNet, BitpackedConvNet,
+from .packed import (PackedLearnedHead, PackedFCLayer, PackedConvLayer, BitpackedNet, BitpackedConvNet,
                      PackedGroupSumHead)
 
 
@@ -27,10 +27,23 @@ def convert_conv_tree_layer(conv):
 
 
 def convert_head(head):
-    from ..heads import GroupSum
+    """GroupSum -> popcount head; LearnedDecoder ``linear`` / ``linfull`` / ``ternary`` ->
+    :class:`PackedLearnedHead` with its effective weight (``convert.py:300-328``);
+    ``sumlinear`` needs batch-norm folding and is refused, as in the reference."""
+    from ..heads import GroupSum, LearnedDecoder
+    from ..functional import ternary_ste
     if isinstance(head, GroupSum):
         return PackedGroupSumHead(head.num_classes, head.tau)
-    raise TypeError(f"no bit-packed form for head {type(head).__name__} in silogic_b200")
+    if isinstance(head, LearnedDecoder):
+        with torch.no_grad():
+            if head.kind in ("linear", "linfull"):
+                return PackedLearnedHead(head.dec.weight.detach().clone(), head.dec.bias.detach().clone())
+            if head.kind == "ternary":
+                return PackedLearnedHead(ternary_ste(head.dec_w).detach().clone(), None)
+            if head.kind == "sumlinear":
+                raise NotImplementedError("sumlinear decoder requires BN folding; use forward_hard")
+        raise ValueError(f"unknown decoder kind {head.kind!r}")
+    raise TypeError(f"no bit-packed form for head {type(head).__name__}")
 
 
 def convert_logic_net(model):

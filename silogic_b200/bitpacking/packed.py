@@ -118,6 +118,33 @@ class PackedGroupSumHead:
         return c.cpu().numpy() if was_np else c
 
 
+class PackedLearnedHead:
+    """Learned linear readout on packed features (``BitpackedLearnedHead``,
+    ``packed_layer.py:574-605``): ``weight`` ``[C, width]``, optional ``bias`` ``[C]``."""
+
+    def __init__(self, weight, bias=None):
+        self.weight = torch.as_tensor(weight, dtype=torch.float32)
+        self.bias = None if bias is None else torch.as_tensor(bias, dtype=torch.float32)
+        self.num_classes = self.weight.shape[0]
+
+    def to(self, device):
+        self.weight = self.weight.to(device)
+        self.bias = self.bias.to(device) if self.bias is not None else None
+        return self
+
+    def apply(self, t, B):
+        """Packed CUDA ``[width, ldw]`` -> fp32 logits ``[B, C]`` on the GPU."""
+        t = t.reshape(-1, t.shape[-1])
+        if self.weight.device != t.device:
+            self.to(t.device)
+        return _hard.packed_linear(t, self.weight, self.bias, B)
+
+    def forward(self, x, B):
+        t, nw, was_np = _packed_in(x)
+        out = self.apply(t, B)
+        return out.cpu().numpy() if was_np else out
+
+
 class BitpackedNet:
     """End-to-end bit-packed ``LogicNet`` on the GPU.  ``net(x)`` with ``x`` ``[B, in]``
     uint8 -> ``[B, num_classes]`` float32 = counts / tau (``packed_model.py:75-102``)."""
@@ -151,7 +178,10 @@ class BitpackedNet:
                 self._graphs.pop(next(iter(self._graphs)))
             static = torch.empty(x.shape, dtype=x.dtype, device=self.device)
             static.copy_(x)
-            g = HardGraph(self.plan, static, thresholds, mode, tau=self.head.tau)
+            if isinstance(self.head, PackedLearnedHead):
+                g = HardGraph(self.plan, static, thresholds, mode, head=self.head)
+            else:
+                g = HardGraph(self.plan, static, thresholds, mode, tau=self.head.tau)
             self._graphs[key] = g
         return g
 
@@ -165,7 +195,7 @@ class BitpackedNet:
         if getattr(self, "_copy_stream", None) is None:
             self._copy_stream = torch.cuda.Stream(dev)
         cs = self._copy_stream
-        logits = torch.empty((B, self.plan.num_classes), dtype=torch.float32, device=dev)
+        logits = torch.empty((B, self.head.num_classes), dtype=torch.float32, device=dev)
         freed = [None, None]          # replay k no longer reads its static input
         cs.wait_stream(main)
         for i, s0 in enumerate(range(0, B, sb)):
@@ -207,12 +237,12 @@ class BitpackedNet:
             logits = g.logits.clone()
         else:
             t = t.to(self.device, non_blocking=True)
-            if thresholds is None:
-                counts = self.plan.counts(t)
+            h = (self.plan.pack_input(t) if thresholds is None
+                 else _hard.thermo_pack(t, thresholds, mode=mode))
+            if isinstance(self.head, PackedLearnedHead):
+                logits = self.head.apply(self.plan.run_packed(h), t.shape[0])
             else:
-                counts = self.plan.counts_from_packed(
-                    _hard.thermo_pack(t, thresholds, mode=mode), t.shape[0])
-            logits = counts.float() / self.head.tau
+                logits = self.plan.counts_from_packed(h, t.shape[0]).float() / self.head.tau
         return logits.cpu().numpy() if was_np else logits
 
     def forward(self, x):

@@ -120,11 +120,13 @@ class HardGraph:
     optionally names the int32 ``[B, num_classes]`` counts buffer to fill.
     ``thresholds`` / ``mode`` select thermometer input as in ``_hard.thermo_pack``
     (``None``: ``x`` is already binary).  ``tau`` adds a float32 ``logits`` output
-    ``counts / tau`` to the graph.
+    ``counts / tau`` to the graph; ``head`` (a ``PackedLearnedHead``) replaces GroupSum
+    and produces ``logits`` only.
     """
 
-    def __init__(self, plan, x, thresholds=None, mode=0, out=None, tau=None):
+    def __init__(self, plan, x, thresholds=None, mode=0, out=None, tau=None, head=None):
         self.plan, self.x, self.thresholds, self.mode, self.tau = plan, x, thresholds, mode, tau
+        self.head = head     # a learned bit-packed readout replacing GroupSum (logits only)
         self._out = out
         dev = x.device
         side = torch.cuda.Stream(dev)
@@ -143,6 +145,8 @@ class HardGraph:
             h = self.plan.pack_input(self.x)
         else:
             h = _hard.thermo_pack(self.x, self.thresholds, mode=self.mode)
+        if self.head is not None:
+            return None, self.head.apply(self.plan.run_packed(h), B)
         counts = self.plan.counts_from_packed(h, B, out=self._out)
         logits = counts.float() / self.tau if self.tau is not None else None
         return counts, logits

@@ -331,6 +331,54 @@ groupsum_kernel(const uint4* __restrict__ x, int64_t G, int64_t rows_per_split, 
     }
 }
 
+// ------------------------------------------------------- learned linear head
+// logits[b, c] = bias[c] + sum_f W[c, f] * bit_f(b) on packed features.  CTA = one
+// 64-sample column (staged in shared memory) x 32 classes; warp = 4 classes, lane =
+// samples j and j + 32, so each feature word and each bit extraction serve 4 classes.
+constexpr int PL_CPW = 4;   // classes per warp
+
+__global__ void __launch_bounds__(256)
+packed_linear_kernel(const uint64_t* __restrict__ x, int64_t width, int64_t ldw, int64_t B,
+                     const float* __restrict__ W, const float* __restrict__ bias, int C,
+                     float* __restrict__ out) {
+    extern __shared__ uint64_t pl_col[];
+    const int64_t w = blockIdx.x;
+    for (int64_t f = threadIdx.x; f < width; f += blockDim.x) pl_col[f] = __ldg(&x[f * ldw + w]);
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c0 = (blockIdx.y * 8 + warp) * PL_CPW;
+    if (c0 >= C) return;
+    float acc[PL_CPW][2];
+    const float* wr[PL_CPW];
+#pragma unroll
+    for (int k = 0; k < PL_CPW; ++k) {
+        acc[k][0] = acc[k][1] = 0.f;
+        wr[k] = W + (int64_t)min(c0 + k, C - 1) * width;
+    }
+    for (int64_t f = 0; f < width; ++f) {
+        const uint64_t v = pl_col[f];
+        const float b0 = (float)((uint32_t)(v >> lane) & 1u);
+        const float b1 = (float)((uint32_t)(v >> (lane + 32)) & 1u);
+#pragma unroll
+        for (int k = 0; k < PL_CPW; ++k) {
+            const float wt = __ldg(wr[k] + f);
+            acc[k][0] = fmaf(b0, wt, acc[k][0]);
+            acc[k][1] = fmaf(b1, wt, acc[k][1]);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < PL_CPW; ++k) {
+        const int c = c0 + k;
+        if (c >= C) break;
+        const float bb = bias ? bias[c] : 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int64_t b = w * 64 + lane + 32 * h;
+            if (b < B) out[b * C + c] = acc[k][h] + bb;
+        }
+    }
+}
+
 }  // namespace slg
 
 using namespace slg;
@@ -463,4 +511,22 @@ extern "C" int slg_groupsum(const uint64_t* x, int64_t width, int64_t ldw, int64
     else if (per < (1 << 10)) groupsum_kernel<10><<<grid, 256, 0, st>>>(xs, G, rps, per, nvec, B, num_classes, counts);
     else groupsum_kernel<16><<<grid, 256, 0, st>>>(xs, G, rps, per, nvec, B, num_classes, counts);
     return check_launch("slg_groupsum");
+}
+
+extern "C" int slg_packed_linear(const uint64_t* x, int64_t width, int64_t ldw, int64_t B,
+                                 const float* W, const float* bias, int32_t num_classes,
+                                 float* out, void* stream) {
+    if (width <= 0 || B < 0 || num_classes <= 0 || ldw < cdiv(B, 64))
+        return set_error(SLG_ERR_ARG, "slg_packed_linear: bad sizes");
+    if (width * (int64_t)sizeof(uint64_t) > 200 * 1024)
+        return set_error(SLG_ERR_UNSUPPORTED, "slg_packed_linear: width %lld over 25,600", (long long)width);
+    if (B == 0) return SLG_OK;
+    if (!x || !W || !out) return set_error(SLG_ERR_ARG, "slg_packed_linear: null pointer");
+    const int64_t nw = cdiv(B, 64);
+    if (nw > 0x7fffffffLL) return set_error(SLG_ERR_ARG, "slg_packed_linear: batch too large");
+    const size_t smem = (size_t)width * sizeof(uint64_t);
+    cudaFuncSetAttribute(packed_linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dim3 grid((unsigned)nw, (unsigned)cdiv(num_classes, 8 * PL_CPW));
+    packed_linear_kernel<<<grid, 256, smem, as_stream(stream)>>>(x, width, ldw, B, W, bias, num_classes, out);
+    return check_launch("slg_packed_linear");
 }

@@ -165,7 +165,12 @@ class LinearNode(Node):
 
 
 class PolynomialNode(Node):
-    """Degree-``d`` multilinear polynomial node (hard path only in this package)."""
+    """Degree-``d`` multilinear polynomial node ``sigmoid(sum_s theta_s prod_{j in s} a_j)``.
+
+    The soft kernels evaluate it in the Walsh form: with ``a_j = (u_j + 1) / 2``,
+    ``prod_{j in s} a_j = 2^-|s| sum_{M subset s} prod_{j in M} u_j``, so
+    ``theta_walsh = theta @ T`` with ``T[s, M] = 2^-|s|`` for ``M`` a subset of ``s``
+    (a fixed linear map, differentiated by autograd) and ``inv_tau = 1``."""
 
     kind, param_name = "polynomial", "theta"
 
@@ -183,6 +188,21 @@ class PolynomialNode(Node):
                 mask[i, j] = 1.0
         self.register_buffer("mono_mask", mask)
         self.theta = nn.Parameter(torch.randn(out_dim, len(subs)) * 0.1)
+        T = torch.zeros(len(subs), 1 << arity)
+        for i, sub in enumerate(subs):
+            S = sum(1 << j for j in sub)
+            M = S
+            while True:                      # every subset M of S
+                T[i, M] += 2.0 ** -len(sub)
+                if M == 0:
+                    break
+                M = (M - 1) & S
+        self.register_buffer("_to_walsh", T, persistent=False)
+
+    def walsh_theta(self):
+        """``[out, 2^arity]`` coefficients of the same function in the ``u = 2a - 1``
+        monomial basis (index = subset bitmask), for the Walsh-form soft kernels."""
+        return self.theta @ self._to_walsh
 
     @torch.no_grad()
     def residual_init(self, p):

@@ -321,3 +321,27 @@ def test_chain_encode_records_on_device():
     o = np.arange(100, dtype=np.uint32)
     ref[:100] = o | (o << 14) | np.uint32(0xA << 28)
     np.testing.assert_array_equal(rec, ref)
+
+
+@pytest.mark.parametrize("decoder", ["linear", "linfull", "ternary"])
+def test_learned_decoder_bitpacked_head(decoder):
+    """BitpackedNet with a learned readout: the packed-feature linear head equals the
+    model's own forward_hard (unpacked bits @ W.T + b); ternary weights are exact."""
+    import silogic_b200 as S
+    from silogic_b200.bitpacking import convert_logic_net
+    torch.manual_seed(4)
+    m = S.LogicNet(100, 320, 2, node="walsh", connectome="topk", k=8, decoder=decoder, seed=4)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.normal_()
+    m = m.to(dev)
+    x = (torch.rand(333, 100, generator=torch.Generator().manual_seed(8)) < 0.3).to(torch.uint8)
+    ref = m.forward_hard(x.to(dev).float()).cpu().numpy()
+    bp = convert_logic_net(m)
+    for graphs in (True, False):
+        bp.graphs = graphs
+        got = bp(x.numpy())
+        if decoder == "ternary":
+            np.testing.assert_array_equal(got, ref)
+        else:
+            np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-4)

@@ -149,7 +149,12 @@ def oracle_soft(ctor, kw, m, x, rmat, pool_index=None):
          tau=5.0, seed=3),
     dict(in_dim=300, width=500, depth=2, node="linear", arity=3, connectome="topk", k=4, tau=5.0,
          seed=4),
-], ids=["walsh_topk8", "gate16_fixed", "gate16_topk16", "multilinear6", "linear3"])
+    dict(in_dim=300, width=500, depth=2, node="polynomial", arity=3, degree=2, connectome="topk",
+         k=4, tau=5.0, seed=5),
+    dict(in_dim=300, width=400, depth=2, node="polynomial", arity=4, connectome="fixed", tau=5.0,
+         seed=6, degree=4),
+], ids=["walsh_topk8", "gate16_fixed", "gate16_topk16", "multilinear6", "linear3", "poly3_d2",
+        "poly4_full"])
 @pytest.mark.parametrize("B", [1, 515])
 def test_fc_soft_vs_oracle(kw, B):
     m = _rand_model("LogicNet", kw, 11)
