@@ -10,7 +10,10 @@ the layer kernels.
 import torch
 
 from . import _hard
-from ._lib import call, lib, ptr, require_cuda, stream_ptr
+from . import _ops  # noqa: F401  (registers the torch.ops.silogic_b200 custom ops)
+from ._lib import require_cuda
+
+OPS = torch.ops.silogic_b200
 
 NODE_ID = {"gate16": 0, "walsh": 1, "multilinear": 2, "hybrid": 3, "linear": 4}
 
@@ -25,41 +28,23 @@ class ToFeatureMajor(torch.autograd.Function):
     def forward(ctx, x):
         require_cuda(x)
         B = x.shape[0]
-        x2 = x.reshape(B, -1).float().contiguous()
-        F = x2.shape[1]
-        ldb = ldb_for(B)
-        out = torch.empty((F, ldb), dtype=torch.float32, device=x.device)
-        call("slg_to_feature_major", ptr(x2), B, F, ptr(out), ldb, stream_ptr(x.device))
         ctx.shape = x.shape
-        return out
+        return OPS.to_feature_major(x.reshape(B, -1), ldb_for(B))
 
     @staticmethod
     def backward(ctx, g):
-        B = ctx.shape[0]
-        g = g.contiguous()
-        F, ldb = g.shape
-        out = torch.empty((B, F), dtype=torch.float32, device=g.device)
-        call("slg_from_feature_major", ptr(g), F, ldb, B, ptr(out), stream_ptr(g.device))
-        return out.view(ctx.shape)
+        return OPS.from_feature_major(g, ctx.shape[0]).view(ctx.shape)
 
 
 class FromFeatureMajor(torch.autograd.Function):
     @staticmethod
     def forward(ctx, xt, B):
-        xt = xt.contiguous()
-        F, ldb = xt.shape
-        out = torch.empty((B, F), dtype=torch.float32, device=xt.device)
-        call("slg_from_feature_major", ptr(xt), F, ldb, B, ptr(out), stream_ptr(xt.device))
-        ctx.ldb = ldb
-        return out
+        ctx.ldb = xt.shape[1]
+        return OPS.from_feature_major(xt, B)
 
     @staticmethod
     def backward(ctx, g):
-        g = g.float().contiguous()
-        B, F = g.shape
-        out = torch.empty((F, ctx.ldb), dtype=torch.float32, device=g.device)
-        call("slg_to_feature_major", ptr(g), B, F, ptr(out), ctx.ldb, stream_ptr(g.device))
-        return out, None
+        return OPS.to_feature_major(g, ctx.ldb), None
 
 
 # --------------------------------------------------------------- FC layer
@@ -110,37 +95,29 @@ class FCSoft(torch.autograd.Function):
     """Feature-major soft FC layer: xt [in, ldb] -> yt [out, ldb]."""
 
     @staticmethod
+    def _args(meta):
+        return (meta["K"], meta["ste"], meta["node"], meta["arity"], meta["gate_hard"],
+                float(meta["inv_tau"]), meta["out_dim"], meta["wire_r"])
+
+    @staticmethod
     def forward(ctx, xt, params, conn, meta):
         require_cuda(xt)
         xt = xt.contiguous()
         params = params.float().contiguous()
         connc = conn.float().contiguous() if conn is not None else None
-        in_dim, ldb = xt.shape
-        y = torch.empty((meta["out_dim"], ldb), dtype=torch.float32, device=xt.device)
-        call("slg_fc_soft_fwd", ptr(xt), in_dim, ldb, ptr(meta["cand"]), ptr(connc), meta["K"],
-             meta["ste"], meta["node"], meta["arity"], ptr(params), meta["gate_hard"],
-             meta["inv_tau"], meta["out_dim"], meta["wire_r"], ptr(y), stream_ptr(xt.device))
+        y = OPS.fc_soft_fwd(xt, meta["cand"], connc, params, *FCSoft._args(meta))
         ctx.save_for_backward(xt, params, connc)
         ctx.meta = meta
-        ctx.has_conn = conn is not None
         return y
 
     @staticmethod
     def backward(ctx, gy):
         xt, params, connc = ctx.saved_tensors
         m = ctx.meta
-        gy = gy.contiguous()
-        in_dim, ldb = xt.shape
-        gx = torch.zeros_like(xt) if ctx.needs_input_grad[0] else None
-        gparams = torch.empty_like(params)
-        gconn = torch.empty_like(connc) if connc is not None else None
-        nbytes = lib().slg_fc_soft_workspace_bytes(ldb, m["K"], m["node"], m["arity"], m["out_dim"])
-        ws = torch.empty(max(nbytes, 4) // 4 + 1, dtype=torch.float32, device=xt.device)
-        call("slg_fc_soft_bwd", ptr(xt), in_dim, ldb, ptr(m["cand"]), ptr(connc), m["K"], m["ste"],
-             m["node"], m["arity"], ptr(params), m["gate_hard"], m["inv_tau"], m["out_dim"],
-             m["wire_r"], ptr(gy), ptr(gx), ptr(gconn), ptr(gparams), ptr(ws), ws.numel() * 4,
-             stream_ptr(xt.device))
-        return gx, gparams, gconn, None
+        gx, gparams, gconn = OPS.fc_soft_bwd(xt, m["cand"], connc, params, *FCSoft._args(m), gy,
+                                             bool(ctx.needs_input_grad[0]))
+        return (gx if ctx.needs_input_grad[0] else None, gparams,
+                gconn if connc is not None else None, None)
 
 
 def fc_layer_fm(layer, xt, wire_r=0):
@@ -175,21 +152,13 @@ class GroupSumSoft(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, xt, B, C, tau, ste):
-        xt = xt.contiguous()
-        W, ldb = xt.shape
-        out = torch.empty((B, C), dtype=torch.float32, device=xt.device)
-        call("slg_groupsum_soft_fwd", ptr(xt), W, ldb, B, C, float(tau), int(ste), ptr(out),
-             stream_ptr(xt.device))
-        ctx.dims = (W, ldb, B, C, float(tau))
-        return out
+        ctx.dims = (xt.shape[0], xt.shape[1], float(tau))
+        return OPS.groupsum_soft_fwd(xt, B, C, float(tau), int(ste))
 
     @staticmethod
     def backward(ctx, g):
-        W, ldb, B, C, tau = ctx.dims
-        g = g.float().contiguous()
-        gx = torch.empty((W, ldb), dtype=torch.float32, device=g.device)
-        call("slg_groupsum_soft_bwd", ptr(g), W, ldb, B, C, tau, ptr(gx), stream_ptr(g.device))
-        return gx, None, None, None, None
+        W, ldb, tau = ctx.dims
+        return OPS.groupsum_soft_bwd(g, W, ldb, tau), None, None, None, None
 
 
 def group_sum_forward(x, num_classes, tau, feature_ste):
@@ -276,26 +245,23 @@ class ConvSoft(torch.autograd.Function):
     """Feature-major conv tree block (+ OR-pool): xt [C*H*W, ldb] -> [n*Hp*Wp, ldb]."""
 
     @staticmethod
+    def _args(meta):
+        return (meta["K"], meta["ste"], meta["node"], meta["arity"], meta["depth"],
+                meta["gate_hard"], float(meta["inv_tau"]), meta["kernel"], meta["pad"],
+                meta["n_out"], meta["wire_r"], meta["pool"])
+
+    @staticmethod
     def forward(ctx, xt, params, conn, meta, shape):
         require_cuda(xt)
         xt = xt.contiguous()
         params = params.float().contiguous()
         connc = conn.float().contiguous() if conn is not None else None
         C, H, W = shape
-        ldb = xt.shape[-1]
-        Ho = H + 2 * meta["pad"] - meta["kernel"] + 1
-        Wo = W + 2 * meta["pad"] - meta["kernel"] + 1
-        Hp, Wp = Ho // meta["pool"], Wo // meta["pool"]
-        y = torch.empty((meta["n_out"] * Hp * Wp, ldb), dtype=torch.float32, device=xt.device)
         # keep each pooled output's window argmax for the backward (1 byte per output)
         # instead of re-evaluating all the window's trees there
-        arg = None
-        if SAVE_POOL_ARGMAX and meta["pool"] > 1 and any(ctx.needs_input_grad[:3]):
-            arg = torch.empty((meta["n_out"] * Hp * Wp, ldb), dtype=torch.uint8, device=xt.device)
-        call("slg_conv_soft_fwd", ptr(xt), C, H, W, ldb, ptr(meta["cand"]), ptr(connc), meta["K"],
-             meta["ste"], meta["node"], meta["arity"], meta["depth"], ptr(params), meta["gate_hard"],
-             meta["inv_tau"], meta["kernel"], meta["pad"], meta["n_out"], meta["wire_r"],
-             meta["pool"], ptr(y), ptr(arg), stream_ptr(xt.device))
+        keep = bool(SAVE_POOL_ARGMAX and meta["pool"] > 1 and any(ctx.needs_input_grad[:3]))
+        y, arg = OPS.conv_soft_fwd(xt, C, H, W, meta["cand"], connc, params, *ConvSoft._args(meta),
+                                   keep)
         ctx.save_for_backward(xt, params, connc, arg)
         ctx.meta, ctx.shape = meta, shape
         return y
@@ -305,20 +271,11 @@ class ConvSoft(torch.autograd.Function):
         xt, params, connc, arg = ctx.saved_tensors
         m = ctx.meta
         C, H, W = ctx.shape
-        ldb = xt.shape[-1]
-        gy = gy.contiguous()
-        gx = torch.zeros_like(xt) if ctx.needs_input_grad[0] else None
-        gparams = torch.empty_like(params)
-        gconn = torch.empty_like(connc) if connc is not None else None
-        nbytes = lib().slg_conv_soft_workspace_bytes(H, W, ldb, m["K"], m["node"], m["arity"],
-                                                     m["depth"], m["kernel"], m["pad"], m["pool"],
-                                                     m["n_out"])
-        ws = torch.empty(max(nbytes, 4) // 4 + 1, dtype=torch.float32, device=xt.device)
-        call("slg_conv_soft_bwd", ptr(xt), C, H, W, ldb, ptr(m["cand"]), ptr(connc), m["K"], m["ste"],
-             m["node"], m["arity"], m["depth"], ptr(params), m["gate_hard"], m["inv_tau"],
-             m["kernel"], m["pad"], m["n_out"], m["wire_r"], m["pool"], ptr(gy), ptr(arg), ptr(gx),
-             ptr(gconn), ptr(gparams), ptr(ws), ws.numel() * 4, stream_ptr(xt.device))
-        return gx, gparams, gconn, None, None
+        gx, gparams, gconn = OPS.conv_soft_bwd(xt, C, H, W, m["cand"], connc, params,
+                                               *ConvSoft._args(m), gy, arg,
+                                               bool(ctx.needs_input_grad[0]))
+        return (gx if ctx.needs_input_grad[0] else None, gparams,
+                gconn if connc is not None else None, None, None)
 
 
 def conv_block_fm(conv, xt, shape, wire_r=0, pool=1):
@@ -371,21 +328,14 @@ class OrPoolSoft(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, size):
         x = x.float().contiguous()
-        B, C, H, W = x.shape
-        y = torch.empty((B, C, H // size, W // size), dtype=torch.float32, device=x.device)
-        call("slg_or_pool_fwd", ptr(x), B * C, H, W, size, ptr(y), stream_ptr(x.device))
         ctx.save_for_backward(x)
         ctx.size = size
-        return y
+        return OPS.or_pool_fwd(x, size)
 
     @staticmethod
     def backward(ctx, gy):
         (x,) = ctx.saved_tensors
-        B, C, H, W = x.shape
-        gy = gy.contiguous()
-        gx = torch.zeros_like(x)
-        call("slg_or_pool_bwd", ptr(x), ptr(gy), B * C, H, W, ctx.size, ptr(gx), stream_ptr(x.device))
-        return gx, None
+        return OPS.or_pool_bwd(x, gy, ctx.size), None
 
 
 def or_pool(x, size):
@@ -405,25 +355,15 @@ class ThermometerSoft(torch.autograd.Function):
     def forward(ctx, x, thr, scale):
         x = x.float().contiguous()
         thr = thr.float().contiguous()
-        B, F = x.shape
-        T = thr.shape[1]
-        out = torch.empty((B, F * T), dtype=torch.float32, device=x.device)
-        call("slg_thermo_soft_fwd", ptr(x), ptr(thr), B, F, T, ptr(out), stream_ptr(x.device))
         ctx.save_for_backward(x, thr)
         ctx.scale = float(scale)
-        return out
+        return OPS.thermo_soft_fwd(x, thr)
 
     @staticmethod
     def backward(ctx, g):
         x, thr = ctx.saved_tensors
-        B, F = x.shape
-        T = thr.shape[1]
-        g = g.float().contiguous()
-        gx = torch.zeros_like(x) if ctx.needs_input_grad[0] else None
-        gthr = torch.zeros_like(thr)
-        call("slg_thermo_soft_bwd", ptr(x), ptr(thr), ptr(g), B, F, T, ctx.scale, ptr(gx),
-             ptr(gthr), stream_ptr(x.device))
-        return gx, gthr, None
+        gx, gthr = OPS.thermo_soft_bwd(x, thr, g, ctx.scale, bool(ctx.needs_input_grad[0]))
+        return (gx if ctx.needs_input_grad[0] else None), gthr, None
 
 
 def thermometer_forward(x, thresholds, scale):

@@ -308,3 +308,31 @@ def test_conv_backward_with_saved_pool_argmax_matches_recompute():
             SS.SAVE_POOL_ARGMAX = True
     for a, b in zip(*grads):
         torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("ctor", ["LogicNet", "LogicTreeNet"])
+def test_torch_compile_traces_the_custom_ops(ctor):
+    """The kernels are torch.library custom ops with fake implementations: torch.compile
+    (AOT autograd, no code generation) traces forward + backward of a whole network and
+    gives the eager results."""
+    import silogic_b200 as S
+    torch.manual_seed(0)
+    if ctor == "LogicNet":
+        m = S.LogicNet(64, 200, 2, node="walsh", connectome="topk", k=8, tau=10.0, seed=0)
+        x = (torch.rand(50, 64) < 0.3).float()
+    else:
+        m = S.LogicTreeNet(in_channels=6, in_hw=8, channels=[16, 32], head_widths=[80],
+                           tree_depth=2, node="gate16", tau=20.0, seed=0)
+        x = (torch.rand(50, 6, 8, 8) < 0.5).float()
+    m = m.to(dev).train()
+    x = x.to(dev)
+    eager_out = m(x)
+    eager_out.sum().backward()
+    ref = [p.grad.clone() for p in m.parameters()]
+    m.zero_grad()
+    cm = torch.compile(m, backend="aot_eager", fullgraph=True)
+    out = cm(x)
+    out.sum().backward()
+    torch.testing.assert_close(out, eager_out, rtol=1e-6, atol=1e-6)
+    for p, r in zip(m.parameters(), ref):
+        torch.testing.assert_close(p.grad, r, rtol=1e-5, atol=1e-6)
