@@ -3,7 +3,8 @@
 Each op wraps one C-ABI entry point functionally (new output tensors, no mutation of
 its inputs) and has a fake (meta) implementation that only computes shapes, so
 ``torch.compile`` / ``torch.export`` can trace the autograd Functions of ``_soft`` that
-call them without breaking the graph.  Absent optional outputs are returned as empty
+call them without breaking the graph (:func:`op` picks the registered op while tracing
+and the plain function in eager mode).  Absent optional outputs are returned as empty
 tensors (custom ops cannot return ``None``).
 """
 from typing import Optional, Tuple
@@ -12,6 +13,27 @@ import torch
 from torch import Tensor
 
 from ._lib import call, lib, ptr, require_cuda, stream_ptr
+
+
+#: the undecorated implementations, called directly in eager mode: the custom-op
+#: dispatcher costs tens of microseconds a call, which small soft steps would notice
+IMPL = {}
+
+
+def _op(name):
+    """Register ``fn`` as ``torch.ops.silogic_b200.<name>`` and keep the raw function."""
+    def deco(fn):
+        IMPL[name] = fn
+        return torch.library.custom_op(f"silogic_b200::{name}", mutates_args=())(fn)
+    return deco
+
+
+def op(name):
+    """The op to call: the registered custom op while torch.compile traces (so the graph
+    holds an opaque node with a fake implementation), the raw function otherwise."""
+    if torch.compiler.is_compiling():
+        return getattr(torch.ops.silogic_b200, name)
+    return IMPL[name]
 
 
 def _none_if_empty(t):
@@ -23,7 +45,7 @@ def _empty(device, dtype=torch.float32):
 
 
 # ------------------------------------------------------------- transposes
-@torch.library.custom_op("silogic_b200::to_feature_major", mutates_args=())
+@_op("to_feature_major")
 def to_feature_major(x: Tensor, ldb: int) -> Tensor:
     """``[B, F]`` -> ``[F, ldb]`` fp32, padding columns zero."""
     require_cuda(x)
@@ -39,7 +61,7 @@ def _(x, ldb):
     return x.new_empty((x.shape[1], ldb), dtype=torch.float32)
 
 
-@torch.library.custom_op("silogic_b200::from_feature_major", mutates_args=())
+@_op("from_feature_major")
 def from_feature_major(xt: Tensor, B: int) -> Tensor:
     """``[F, ldb]`` -> ``[B, F]`` fp32."""
     require_cuda(xt)
@@ -56,7 +78,7 @@ def _(xt, B):
 
 
 # --------------------------------------------------------------- FC layer
-@torch.library.custom_op("silogic_b200::fc_soft_fwd", mutates_args=())
+@_op("fc_soft_fwd")
 def fc_soft_fwd(xt: Tensor, cand: Tensor, conn: Optional[Tensor], params: Tensor, K: int,
                 ste: int, node: int, arity: int, gate_hard: int, inv_tau: float, out_dim: int,
                 wire_r: int) -> Tensor:
@@ -73,7 +95,7 @@ def _(xt, cand, conn, params, K, ste, node, arity, gate_hard, inv_tau, out_dim, 
     return xt.new_empty((out_dim, xt.shape[1]))
 
 
-@torch.library.custom_op("silogic_b200::fc_soft_bwd", mutates_args=())
+@_op("fc_soft_bwd")
 def fc_soft_bwd(xt: Tensor, cand: Tensor, conn: Optional[Tensor], params: Tensor, K: int,
                 ste: int, node: int, arity: int, gate_hard: int, inv_tau: float, out_dim: int,
                 wire_r: int, gy: Tensor, need_gx: bool) -> Tuple[Tensor, Tensor, Tensor]:
@@ -102,7 +124,7 @@ def _(xt, cand, conn, params, K, ste, node, arity, gate_hard, inv_tau, out_dim, 
 
 
 # ---------------------------------------------------------------- GroupSum
-@torch.library.custom_op("silogic_b200::groupsum_soft_fwd", mutates_args=())
+@_op("groupsum_soft_fwd")
 def groupsum_soft_fwd(xt: Tensor, B: int, C: int, tau: float, ste: int) -> Tensor:
     require_cuda(xt)
     xt = xt.contiguous()
@@ -117,7 +139,7 @@ def _(xt, B, C, tau, ste):
     return xt.new_empty((B, C))
 
 
-@torch.library.custom_op("silogic_b200::groupsum_soft_bwd", mutates_args=())
+@_op("groupsum_soft_bwd")
 def groupsum_soft_bwd(g: Tensor, W: int, ldb: int, tau: float) -> Tensor:
     require_cuda(g)
     g = g.float().contiguous()
@@ -138,7 +160,7 @@ def _conv_out(C, H, W, kernel, pad, pool, n_out):
     return n_out * (Ho // pool) * (Wo // pool)
 
 
-@torch.library.custom_op("silogic_b200::conv_soft_fwd", mutates_args=())
+@_op("conv_soft_fwd")
 def conv_soft_fwd(xt: Tensor, C: int, H: int, W: int, cand: Tensor, conn: Optional[Tensor],
                   params: Tensor, K: int, ste: int, node: int, arity: int, depth: int,
                   gate_hard: int, inv_tau: float, kernel: int, pad: int, n_out: int, wire_r: int,
@@ -164,7 +186,7 @@ def _(xt, C, H, W, cand, conn, params, K, ste, node, arity, depth, gate_hard, in
     return y, arg
 
 
-@torch.library.custom_op("silogic_b200::conv_soft_bwd", mutates_args=())
+@_op("conv_soft_bwd")
 def conv_soft_bwd(xt: Tensor, C: int, H: int, W: int, cand: Tensor, conn: Optional[Tensor],
                   params: Tensor, K: int, ste: int, node: int, arity: int, depth: int,
                   gate_hard: int, inv_tau: float, kernel: int, pad: int, n_out: int, wire_r: int,
@@ -198,7 +220,7 @@ def _(xt, C, H, W, cand, conn, params, K, ste, node, arity, depth, gate_hard, in
 
 
 # ------------------------------------------------------------------ OrPool
-@torch.library.custom_op("silogic_b200::or_pool_fwd", mutates_args=())
+@_op("or_pool_fwd")
 def or_pool_fwd(x: Tensor, size: int) -> Tensor:
     require_cuda(x)
     x = x.float().contiguous()
@@ -214,7 +236,7 @@ def _(x, size):
     return x.new_empty((B, C, H // size, W // size), dtype=torch.float32)
 
 
-@torch.library.custom_op("silogic_b200::or_pool_bwd", mutates_args=())
+@_op("or_pool_bwd")
 def or_pool_bwd(x: Tensor, gy: Tensor, size: int) -> Tensor:
     require_cuda(x)
     B, C, H, W = x.shape
@@ -230,7 +252,7 @@ def _(x, gy, size):
 
 
 # ---------------------------------------------------------------- encoder
-@torch.library.custom_op("silogic_b200::thermo_soft_fwd", mutates_args=())
+@_op("thermo_soft_fwd")
 def thermo_soft_fwd(x: Tensor, thr: Tensor) -> Tensor:
     require_cuda(x)
     B, F = x.shape
@@ -245,7 +267,7 @@ def _(x, thr):
     return x.new_empty((x.shape[0], x.shape[1] * thr.shape[1]))
 
 
-@torch.library.custom_op("silogic_b200::thermo_soft_bwd", mutates_args=())
+@_op("thermo_soft_bwd")
 def thermo_soft_bwd(x: Tensor, thr: Tensor, g: Tensor, scale: float,
                     need_gx: bool) -> Tuple[Tensor, Tensor]:
     """(gx or empty, gthr)."""

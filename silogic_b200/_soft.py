@@ -10,10 +10,9 @@ the layer kernels.
 import torch
 
 from . import _hard
-from . import _ops  # noqa: F401  (registers the torch.ops.silogic_b200 custom ops)
+from ._ops import op
 from ._lib import require_cuda
 
-OPS = torch.ops.silogic_b200
 
 NODE_ID = {"gate16": 0, "walsh": 1, "multilinear": 2, "hybrid": 3, "linear": 4}
 
@@ -29,22 +28,22 @@ class ToFeatureMajor(torch.autograd.Function):
         require_cuda(x)
         B = x.shape[0]
         ctx.shape = x.shape
-        return OPS.to_feature_major(x.reshape(B, -1), ldb_for(B))
+        return op("to_feature_major")(x.reshape(B, -1), ldb_for(B))
 
     @staticmethod
     def backward(ctx, g):
-        return OPS.from_feature_major(g, ctx.shape[0]).view(ctx.shape)
+        return op("from_feature_major")(g, ctx.shape[0]).view(ctx.shape)
 
 
 class FromFeatureMajor(torch.autograd.Function):
     @staticmethod
     def forward(ctx, xt, B):
         ctx.ldb = xt.shape[1]
-        return OPS.from_feature_major(xt, B)
+        return op("from_feature_major")(xt, B)
 
     @staticmethod
     def backward(ctx, g):
-        return OPS.to_feature_major(g, ctx.ldb), None
+        return op("to_feature_major")(g, ctx.ldb), None
 
 
 # --------------------------------------------------------------- FC layer
@@ -105,7 +104,7 @@ class FCSoft(torch.autograd.Function):
         xt = xt.contiguous()
         params = params.float().contiguous()
         connc = conn.float().contiguous() if conn is not None else None
-        y = OPS.fc_soft_fwd(xt, meta["cand"], connc, params, *FCSoft._args(meta))
+        y = op("fc_soft_fwd")(xt, meta["cand"], connc, params, *FCSoft._args(meta))
         ctx.save_for_backward(xt, params, connc)
         ctx.meta = meta
         return y
@@ -114,7 +113,7 @@ class FCSoft(torch.autograd.Function):
     def backward(ctx, gy):
         xt, params, connc = ctx.saved_tensors
         m = ctx.meta
-        gx, gparams, gconn = OPS.fc_soft_bwd(xt, m["cand"], connc, params, *FCSoft._args(m), gy,
+        gx, gparams, gconn = op("fc_soft_bwd")(xt, m["cand"], connc, params, *FCSoft._args(m), gy,
                                              bool(ctx.needs_input_grad[0]))
         return (gx if ctx.needs_input_grad[0] else None, gparams,
                 gconn if connc is not None else None, None)
@@ -153,12 +152,12 @@ class GroupSumSoft(torch.autograd.Function):
     @staticmethod
     def forward(ctx, xt, B, C, tau, ste):
         ctx.dims = (xt.shape[0], xt.shape[1], float(tau))
-        return OPS.groupsum_soft_fwd(xt, B, C, float(tau), int(ste))
+        return op("groupsum_soft_fwd")(xt, B, C, float(tau), int(ste))
 
     @staticmethod
     def backward(ctx, g):
         W, ldb, tau = ctx.dims
-        return OPS.groupsum_soft_bwd(g, W, ldb, tau), None, None, None, None
+        return op("groupsum_soft_bwd")(g, W, ldb, tau), None, None, None, None
 
 
 def group_sum_forward(x, num_classes, tau, feature_ste):
@@ -260,7 +259,8 @@ class ConvSoft(torch.autograd.Function):
         # keep each pooled output's window argmax for the backward (1 byte per output)
         # instead of re-evaluating all the window's trees there
         keep = bool(SAVE_POOL_ARGMAX and meta["pool"] > 1 and any(ctx.needs_input_grad[:3]))
-        y, arg = OPS.conv_soft_fwd(xt, C, H, W, meta["cand"], connc, params, *ConvSoft._args(meta),
+        y, arg = op("conv_soft_fwd")(xt, C, H, W, meta["cand"], connc, params,
+                                     *ConvSoft._args(meta),
                                    keep)
         ctx.save_for_backward(xt, params, connc, arg)
         ctx.meta, ctx.shape = meta, shape
@@ -271,7 +271,7 @@ class ConvSoft(torch.autograd.Function):
         xt, params, connc, arg = ctx.saved_tensors
         m = ctx.meta
         C, H, W = ctx.shape
-        gx, gparams, gconn = OPS.conv_soft_bwd(xt, C, H, W, m["cand"], connc, params,
+        gx, gparams, gconn = op("conv_soft_bwd")(xt, C, H, W, m["cand"], connc, params,
                                                *ConvSoft._args(m), gy, arg,
                                                bool(ctx.needs_input_grad[0]))
         return (gx if ctx.needs_input_grad[0] else None, gparams,
@@ -330,12 +330,12 @@ class OrPoolSoft(torch.autograd.Function):
         x = x.float().contiguous()
         ctx.save_for_backward(x)
         ctx.size = size
-        return OPS.or_pool_fwd(x, size)
+        return op("or_pool_fwd")(x, size)
 
     @staticmethod
     def backward(ctx, gy):
         (x,) = ctx.saved_tensors
-        return OPS.or_pool_bwd(x, gy, ctx.size), None
+        return op("or_pool_bwd")(x, gy, ctx.size), None
 
 
 def or_pool(x, size):
@@ -357,12 +357,12 @@ class ThermometerSoft(torch.autograd.Function):
         thr = thr.float().contiguous()
         ctx.save_for_backward(x, thr)
         ctx.scale = float(scale)
-        return OPS.thermo_soft_fwd(x, thr)
+        return op("thermo_soft_fwd")(x, thr)
 
     @staticmethod
     def backward(ctx, g):
         x, thr = ctx.saved_tensors
-        gx, gthr = OPS.thermo_soft_bwd(x, thr, g, ctx.scale, bool(ctx.needs_input_grad[0]))
+        gx, gthr = op("thermo_soft_bwd")(x, thr, g, ctx.scale, bool(ctx.needs_input_grad[0]))
         return (gx if ctx.needs_input_grad[0] else None), gthr, None
 
 
