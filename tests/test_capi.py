@@ -58,3 +58,37 @@ def test_bad_arguments_are_rejected(L):
     assert st == 1
     # empty work is a no-op success
     assert L.slg_pack_u8(_p(0), 0, 5, _p(0), 2, _p(0)) == 0
+
+
+def test_chain_planner_runs_on_the_host_and_rejects_bad_wiring():
+    """slg_fc_chain_plan is host code: it runs without a GPU, lays the last layer out in
+    per-class blocks padded to whole warps, and refuses a wiring that reads past the
+    previous layer."""
+    import numpy as np
+    from silogic_b200._hard import CHAIN_MAX_WIDTH
+    P = ctypes.c_void_p
+    in_dim, out, C = 40, 50, 5
+    rng = np.random.default_rng(0)
+    idx = rng.integers(0, in_dim, (out, 2)).astype(np.int32)
+    tt = rng.integers(0, 16, out).astype(np.uint64)
+    outs, wr = np.array([out], np.int64), np.array([0], np.int64)
+    rec = np.zeros(2 * CHAIN_MAX_WIDTH, np.uint32)
+    widths, off = np.zeros(1, np.int32), np.zeros(C + 1, np.int32)
+
+    def plan(idx_arr, reorder):
+        return _lib.lib().slg_fc_chain_plan(in_dim, 1, P(outs.ctypes.data), P(idx_arr.ctypes.data),
+                                           P(tt.ctypes.data), P(wr.ctypes.data), C, reorder,
+                                           P(rec.ctypes.data), CHAIN_MAX_WIDTH,
+                                           P(widths.ctypes.data), P(off.ctypes.data))
+    assert plan(idx, 0) == 0
+    assert widths[0] % 32 == 0 and list(off) == [32 * c for c in range(C + 1)]
+    for c in range(C):                 # each class's 10 nodes sit in its own block
+        r = rec[off[c]:off[c + 1]].astype(np.int64)
+        have = set(zip((r & 0x3fff).tolist(), ((r >> 14) & 0x3fff).tolist(), (r >> 28).tolist()))
+        want = set(zip(idx[10 * c:10 * c + 10, 0].tolist(), idx[10 * c:10 * c + 10, 1].tolist(),
+                       tt[10 * c:10 * c + 10].astype(np.int64).tolist()))
+        assert want <= have
+    bad = idx.copy()
+    bad[3, 1] = in_dim                 # one past the input layer
+    assert plan(bad, 1) != 0
+    assert b"out of range" in _lib.lib().slg_last_error()
