@@ -10,6 +10,36 @@ import torch
 from .. import _hard
 
 
+#: relabel conv output channels for L2 locality (see _order_channels_for_locality)
+LOCALITY_ORDER = True
+
+
+def _order_channels_for_locality(steps):
+    """Relabel the output channels of every conv block that feeds another step so that
+    channels reading the same input channels are adjacent.  The conv kernel walks output
+    channels in order, so neighbouring CTAs then share input planes in L2 instead of
+    fetching them from HBM again; the next step's taps (or the FC head's feature
+    indices) are renamed to match, so the circuit and its outputs are unchanged."""
+    for i, st in enumerate(steps[:-1]):
+        if st["op"] != "conv":
+            continue
+        kk = st["kernel"] * st["kernel"]
+        key = (st["leaf"].long() // kk).min(dim=1).values
+        perm = torch.argsort(key, stable=True)                  # new position -> old channel
+        inv = torch.empty_like(perm)
+        inv[perm] = torch.arange(perm.numel(), device=perm.device)
+        st["leaf"], st["tt"] = st["leaf"][perm].contiguous(), st["tt"][perm].contiguous()
+        nxt = steps[i + 1]
+        if nxt["op"] == "conv":
+            kk2 = nxt["kernel"] * nxt["kernel"]
+            leaf = nxt["leaf"].long()
+            nxt["leaf"] = (inv[leaf // kk2] * kk2 + leaf % kk2).to(torch.int32).contiguous()
+        else:
+            hw = nxt["in_dim"] // st["n"]                         # pooled positions
+            idx = nxt["idx"].long()
+            nxt["idx"] = (inv[idx // hw] * hw + idx % hw).to(nxt["idx"].dtype).contiguous()
+
+
 class HardPlan:
     """Wiring + truth tables of every layer, on the parameters' device."""
 
@@ -64,8 +94,10 @@ class HardPlan:
                                   n=conv.n))
             for layer in model.head_layers:
                 idx, tt = layer.hard_spec()
-                steps.append(dict(op="fc", idx=idx, tt=tt, wire_r=0))
+                steps.append(dict(op="fc", idx=idx, tt=tt, wire_r=0, in_dim=layer.in_dim))
             in_shape = ("conv", first.cin, None, None)
+            if LOCALITY_ORDER and all(st["wire_r"] == 0 for st in steps):
+                _order_channels_for_locality(steps)
         else:
             raise TypeError(f"unsupported model {type(model).__name__}")
         head = model.head
