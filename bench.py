@@ -1,19 +1,23 @@
 """Benchmark of the silogic_b200 hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c1|c2|c3|c4|c5] [--no-soft] [--cpu-sample S]
+                    [--config c1|c2|c3|c4|c5] [--extras c2,..|none] [--no-soft]
+                    [--no-cpu] [--reference-gpu] [--batch B]
 
 Configs are BASELINE.json's (synthetic, seeded inputs; every parameter N(0,1)):
   c1  FC LogicNet 784 -> 8000 x 4, gate16, fixed wiring; hard + soft at B=1024
-  c2  FC LogicNet 784 -> 10000 x 6, Walsh, Top-K 8 (default, the headline);
-      hard bit-packed inference at B=65,536, soft fwd+bwd at B=4,096
+  c2  FC LogicNet 784 -> 10000 x 6, Walsh, Top-K 8; hard bit-packed inference at
+      B=65,536 per GPU, soft fwd+bwd at B=4,096 per GPU (weak scaling)
   c3  LogicTreeNet 3x32x32 thermometer (5 thresholds) -> gate16 trees depth 2,
       channels 128/256/512 + OR-pool, head 1280; B=4,096
   c4  LogicConvNet, learned thermometer (3 bits), multilinear arity-6 trees,
       channels 128/256, head 16000 x 2, STE selection; B=8,192
-  c5  LogicTreeNet 3x32x32 thermometer (31 thresholds), gate16 depth 2, channels
-      1024/2048/4096/8192, head 12800/6400/3200; 1,048,576 samples split across the
-      GPUs (strong scaling), processed in 131,072-sample device chunks
+  c5  (default, the headline: the largest single-GPU config) LogicTreeNet 3x32x32
+      thermometer (31 thresholds), gate16 depth 2, channels 1024/2048/4096/8192,
+      head 12800/6400/3200; 1,048,576 samples split across the GPUs (strong
+      scaling), processed in 131,072-sample device chunks
+With the default c5 headline, c2 (hard + soft) is measured in the same run and
+reported under the key "c2".
 A "step" is one pass of the hard circuit over the per-GPU batch (value); the
 soft fwd+bwd leg (key "soft_fwd_bwd") is one forward + backward of its batch,
 plus one NCCL all-reduce of the parameter gradients when N > 1.  Hard inference
@@ -22,7 +26,13 @@ Timing: CUDA events on the launching stream around each step, L2 flushed (a
 256 MB write read back, untimed) before each step, W >= 3 warm-up steps, barrier +
 synchronize around the timed loop, max over ranks.  "e2e" runs the same work
 through the public API from pinned host memory with the host<->device copies
-inside the timed region.
+inside the timed region.  "parity" compares (untimed) the timed step's counts of
+the first 128 samples with the CPU oracle; "cpu_baseline" times the reference's
+own CPU path (baseline/_ref) on a bounded sample of the same batch and says
+whether its counts equal the GPU's.
+--impl reference times the reference's own CPU path (rank 0 only) on a bounded
+sample per step; --reference-gpu adds the reference's Triton GPU path, timed in
+a child process, under "reference_gpu".
 """
 import argparse
 import json
@@ -403,7 +413,10 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
     # stages it replaces (every FC layer and the GroupSum)
     per_kind["fc_chain"] = per_kind.get("fc_hard", 0.0) + per_kind.get("groupsum", 0.0)
     in_bytes = x_host[:1].numel() * x_host.element_size()
-    return dict(ms=ms, e2e_ms=e2e_ms, kern=kern, per_kind=per_kind,
+    step_device(collective=False)
+    torch.cuda.synchronize()
+    return dict(ms=ms, e2e_ms=e2e_ms, kern=kern, per_kind=per_kind, x_first=x_host,
+                counts_first=counts_all[:chunk].cpu(), enc=enc, model=model,
                 bytes_per_sample=sum(b for _, b in stage), launches_per_step=launches[0] / steps,
                 clocks=clk.summary(), h2d=int(in_bytes * B), d2h=int(B * plan.num_classes * 4))
 
@@ -460,51 +473,259 @@ def run_soft(cfg, B, steps, warmup, rank, ws, dev):
 
 
 # ------------------------------------------------------------ CPU baselines
-_SPEC_CACHE = {}
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 
 
-def cpu_hard_sample(cfg, n_samples, threads=1):
-    """The CPU oracle (numpy bit-packed restatement of the reference's hard path) on a
-    bounded sample: ``threads`` workers over 64-sample-aligned slices."""
-    from concurrent.futures import ThreadPoolExecutor
+def import_reference():
+    """The unmodified reference package installed in baseline/_ref (pure Python:
+    numpy for the bit-packed CPU path, Triton for its GPU path), or None."""
+    if not os.path.isdir(os.path.join(REF_DIR, "silogic")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        import silogic
+    except Exception:
+        return None
+    return silogic
+
+
+def reference_net(silogic, cfg, seed=0):
+    """The config's network built with the REFERENCE's own constructors and the same
+    seeded N(0,1) parameters as build_model (identical state_dicts)."""
+    torch.manual_seed(seed)
+    m = getattr(silogic, cfg["ctor"])(**cfg["kwargs"])
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.copy_(torch.randn(p.shape, generator=g))
+    from silogic.bitpacking import convert_logic_net, convert_logic_conv_net
+    bp = convert_logic_net(m) if cfg["ctor"] == "LogicNet" else convert_logic_conv_net(m)
+    enc = None
+    if cfg["inp"] == "encoder":
+        torch.manual_seed(seed)
+        enc = silogic.LearnedThermometerEncoder(3 * 32 * 32, cfg["bits"])
+    return m, bp, enc
+
+
+def reference_cpu_step(silogic, cfg, bp, enc, x):
+    """One pass of the reference's fastest CPU path over host batch ``x`` through its
+    public API: the input encoding (``binarize_spatial`` / the learned encoder) and
+    ``BitpackedNet`` / ``BitpackedConvNet`` (``bitpacking/packed_model.py``).  Returns
+    integer counts (logits x tau)."""
+    if cfg["inp"] == "bern":
+        xb = x.numpy()
+    elif cfg["inp"] == "image":
+        from silogic.data import binarize_spatial
+        xb = binarize_spatial(x, cfg["thresholds"]).numpy()
+    else:
+        n = x.shape[0]
+        e = enc.forward_hard(x.reshape(n, -1))
+        xb = e.view(n, 3, 32, 32, cfg["bits"]).permute(0, 1, 4, 2, 3).reshape(n, -1, 32, 32).numpy()
+    return np.rint(bp(xb) * cfg["kwargs"]["tau"]).astype(np.int64)
+
+
+def cpu_port_sample(cfg, x):
+    """The numpy restatement of the reference's bit-packed path (oracle/hard.py) on
+    host batch ``x``; returns integer counts."""
     from oracle import hard as OH
     from oracle.spec import net_spec
-    key = (cfg["name"], n_samples)
-    if key not in _SPEC_CACHE:
-        model, enc = build_model(cfg)
-        sd = {k: v.numpy() for k, v in model.state_dict().items()}
-        spec = net_spec(cfg["ctor"], cfg["kwargs"], sd)
-        x = make_input(cfg, n_samples, seed=1).numpy()
-        if cfg["inp"] == "image":
-            x = OH.thermometer_bits(x, cfg["thresholds"])
-        elif cfg["inp"] == "encoder":
-            e = OH.learned_thermometer_bits(x.reshape(n_samples, -1), enc.thresholds.detach().numpy())
-            x = e.reshape(n_samples, 3, 32, 32, cfg["bits"]).transpose(0, 1, 4, 2, 3).reshape(
-                n_samples, -1, 32, 32)
-        _SPEC_CACHE[key] = (spec, x)
-    spec, x = _SPEC_CACHE[key]
-    chunk = max(64, (n_samples // threads) // 64 * 64)
-    parts = [x[i:i + chunk] for i in range(0, n_samples, chunk)]
-    t0 = time.perf_counter()
-    with ThreadPoolExecutor(max_workers=threads) as ex:
-        list(ex.map(lambda p: OH.net_counts(spec, p), parts))
-    dt = time.perf_counter() - t0
-    return n_samples / dt, dt
+    model, enc = build_model(cfg)
+    sd = {k: v.numpy() for k, v in model.state_dict().items()}
+    spec = net_spec(cfg["ctor"], cfg["kwargs"], sd)
+    n = x.shape[0]
+    xn = x.numpy()
+    if cfg["inp"] == "image":
+        xn = OH.thermometer_bits(xn, cfg["thresholds"])
+    elif cfg["inp"] == "encoder":
+        e = OH.learned_thermometer_bits(xn.reshape(n, -1), enc.thresholds.detach().numpy())
+        xn = e.reshape(n, 3, 32, 32, cfg["bits"]).transpose(0, 1, 4, 2, 3).reshape(n, -1, 32, 32)
+    return OH.net_counts(spec, xn)
 
 
-DEFAULT_CPU_SAMPLE = {"c1": 1024, "c2": 4096, "c3": 256, "c4": 128, "c5": 64}
+# bounded CPU samples (about 5-15 s of the reference's CPU path on a 32-core host)
+CPU_SAMPLE = {"c1": 8192, "c2": 65536, "c3": 1024, "c4": 256, "c5": 2048}
+
+
+def cpu_baseline(cfg_key, cfg, x_host, counts):
+    """Time the reference's CPU path (baseline/_ref) on the first samples of the GPU
+    batch and check that it gives the same counts as the GPU; falls back to the numpy
+    port when the reference is not installed."""
+    n = min(CPU_SAMPLE[cfg_key], x_host.shape[0])
+    x = x_host[:n].clone()
+    silogic = import_reference()
+    threads = torch.get_num_threads()
+    if silogic is not None:
+        m, bp, enc = reference_net(silogic, cfg)
+        reference_cpu_step(silogic, cfg, bp, enc, x[:64])         # warm-up
+        t0 = time.perf_counter()
+        ref = reference_cpu_step(silogic, cfg, bp, enc, x)
+        dt = time.perf_counter() - t0
+        kind, what = "reference", ("the reference's own CPU path from baseline/_ref: input "
+                                   "encoding + BitpackedNet/BitpackedConvNet (numpy)")
+    else:
+        t0 = time.perf_counter()
+        ref = cpu_port_sample(cfg, x)
+        dt = time.perf_counter() - t0
+        kind, what, threads = "port", "the numpy restatement of the reference (oracle/hard.py)", 1
+    same = bool(np.array_equal(ref, counts[:n].numpy().astype(np.int64)))
+    return {"value": n / dt, "unit": "samples/s", "cores": threads, "kind": kind,
+            "sample": f"{n} samples of the same batch through {what}, {dt:.2f} s, "
+                      f"torch threads {threads}, host cpus {os.cpu_count()}",
+            "counts_equal_gpu": same}
+
+
+def parity_check(cfg, x_host, counts, n=128):
+    """Untimed: the GPU counts of the first ``n`` samples of the timed batch against the
+    oracle (numpy restatement of the reference's bit-packed path)."""
+    n = min(n, x_host.shape[0])
+    ref = cpu_port_sample(cfg, x_host[:n].clone())
+    got = counts[:n].numpy().astype(np.int64)
+    return {"samples": n, "oracle": "oracle/hard.py", "equal": bool(np.array_equal(ref, got))}
+
+
+def reference_gpu(cfg_key, batch, steps=3, warmup=1):
+    """The reference's own GPU (Triton) bit-packed path on this box, in a child
+    process, as a same-hardware bar: ``BitpackedConvGPUNet`` (conv configs) or
+    ``BitpackedNet`` layers on ``BitpackedGPULayer`` (FC configs)."""
+    cmd = [sys.executable, os.path.abspath(__file__), "--impl", "reference-gpu", "--config", cfg_key,
+           "--batch", str(batch), "--steps", str(steps), "--warmup", str(warmup)]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
+        lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+        if r.returncode == 0 and lines:
+            return json.loads(lines[-1])
+        err = (r.stderr.strip().splitlines() or ["no output"])[-1]
+        return {"unavailable": f"exit {r.returncode}: {err[:300]}"}
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "timed out after 900 s"}
+
+
+def run_reference_gpu(cfg_key, cfg, a):
+    """Child process of reference_gpu(): time the reference's Triton path end to end
+    through its public API (numpy uint8 in, numpy logits out; host packing included,
+    as in the reference's own benchmark harness, bitpacking/benchmark.py)."""
+    silogic = import_reference()
+    if silogic is None:
+        print(json.dumps({"unavailable": "reference not installed in baseline/_ref"}))
+        return
+    from silogic.bitpacking import HAS_TRITON
+    if not HAS_TRITON:
+        print(json.dumps({"unavailable": "reference Triton path not importable on this box"}))
+        return
+    m, bp, enc = reference_net(silogic, cfg)
+    B = a.batch
+    x = make_input(cfg, B, seed=1)
+    if cfg["inp"] == "bern":
+        xb = x.numpy()
+        from silogic.bitpacking.kernels import BitpackedGPULayer
+        from silogic.bitpacking.ops import pack_bits, mask_last_word
+        layers = [BitpackedGPULayer.from_fc_layer(L, "cuda") for L in bp.packed_layers]
+
+        def run():
+            h = torch.from_numpy(pack_bits(xb)).cuda()
+            for L in layers:
+                h = L.forward(h)
+            p = h.cpu().numpy()
+            mask_last_word(p, B)
+            return bp.head.forward(p, B)
+        what = "BitpackedGPULayer per FC layer (Triton) + host pack/head"
+    else:
+        from silogic.bitpacking import BitpackedConvGPUNet
+        from silogic.data import binarize_spatial
+        xb = binarize_spatial(x, cfg["thresholds"]).numpy()
+        gnet = BitpackedConvGPUNet.from_conv_net(bp, 32, 32, "cuda")
+        run = lambda: gnet(xb)
+        what = "BitpackedConvGPUNet (Triton gate trees, torch unfold/OR-pool) + host pack/head"
+    for _ in range(warmup_n(a)):
+        out = run()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(a.steps):
+        t0 = time.perf_counter()
+        out = run()
+        torch.cuda.synchronize()
+        ts.append(time.perf_counter() - t0)
+    counts = np.rint(out * cfg["kwargs"]["tau"]).astype(np.int64)
+    ours_ok = None
+    try:
+        ours_ok = bool(np.array_equal(counts[:128], cpu_port_sample(cfg, x[:128].clone())))
+    except Exception:
+        pass
+    dt = statistics.mean(ts)
+    print(json.dumps({"value": B / dt, "unit": "samples/s", "batch": B, "ms_per_step": dt * 1e3,
+                      "path": what, "timing": "host wall clock around the reference's numpy-in/"
+                      "numpy-out call (its own API), mean of steps", "counts_equal_oracle_128": ours_ok}))
+
+
+def warmup_n(a):
+    return max(1, a.warmup)
+
+
+# ----------------------------------------------------------- one config, ours
+def measure_ours(cfg_key, cfg, a, ws, rank, dev, warmup, with_soft=True, check=True):
+    """Hard (and optionally soft) legs of one config; MAX over ranks of every time."""
+    B = cfg["hard_batch"] // (ws if cfg["scaling"] == "strong" else 1)
+    r = run_hard(cfg, B, a.steps, warmup, rank, ws, dev)
+    soft = None
+    if with_soft and cfg["soft_batch"]:
+        soft = run_soft(cfg, cfg["soft_batch"], a.steps, warmup, rank, ws, dev)
+    ms = torch.tensor([r["ms"], r["e2e_ms"], soft["ms"] if soft else 0.0], device=dev)
+    if ws > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    ms_step, e2e_ms, soft_ms = ms.tolist()
+    hbm, kind = peaks()
+    dom = max(r["kern"], key=lambda k: r["kern"][k][0])
+    dom_ms, dom_n = r["kern"][dom]
+    dom_bytes = r["per_kind"][dom] * B
+    ach = dom_bytes / (dom_ms * 1e-3) / 1e9
+    total = B * ws if cfg["scaling"] == "weak" else cfg["hard_batch"]
+    out = {
+        "value": total / (ms_step * 1e-3), "ms_per_step": ms_step, "B": B, "total": total,
+        "e2e": {"value": total / (e2e_ms * 1e-3), "unit": "samples/s",
+                "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+        "gpu_launches": int(round(r["launches_per_step"] * a.steps)),
+        "roofline": {"kernel": f"slg_{dom} ({dom_n:.0f} launches/step)", "bound": "hbm",
+                     "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                     "peak_kind": kind,
+                     "traffic": NCU_TRAFFIC.get((cfg_key, dom), (None,))[0] if not a.batch else None,
+                     "traffic_source": NCU_TRAFFIC.get((cfg_key, dom), (None, None))[1],
+                     "algorithmic_bytes_per_step": dom_bytes,
+                     "step_frac": r["bytes_per_sample"] * B / (ms_step * 1e-3) / 1e9 / hbm,
+                     "algorithmic_bytes_per_sample": r["bytes_per_sample"]},
+        "kernels_ms_per_step": {k: v[0] for k, v in r["kern"].items()},
+        "clocks": r["clocks"], "r": r,
+    }
+    if soft:
+        Bs = cfg["soft_batch"]
+        ach_s = soft["bytes_per_sample"] * Bs / (soft_ms * 1e-3) / 1e9
+        out["soft_fwd_bwd"] = {
+            "metric": "soft fwd+bwd samples/s", "value": Bs * ws / (soft_ms * 1e-3),
+            "unit": "samples/s", "ms_per_step": soft_ms, "batch_per_gpu": Bs, "dtype": "f32",
+            "roofline": {"bound": "hbm (layer-wise bytes; gathers are L2-bound)",
+                         "achieved": ach_s, "peak": hbm, "unit": "GB/s", "frac": ach_s / hbm,
+                         "algorithmic_bytes_per_sample": soft["bytes_per_sample"]},
+            "collective": "one NCCL all-reduce of all parameter gradients" if ws > 1 else None}
+    if check and rank == 0:
+        out["parity"] = parity_check(cfg, r["x_first"], r["counts_first"])
+    return out
 
 
 # ------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
-    ap.add_argument("--cpu-sample", type=int, default=None)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu"])
+    ap.add_argument("--config", default="c5", choices=sorted(CONFIGS))
+    ap.add_argument("--extras", default=None,
+                    help="comma list of further configs measured in the same run "
+                         "(default: c2 when the headline is c5; 'none' for none)")
     ap.add_argument("--no-soft", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--reference-gpu", action="store_true",
+                    help="also time the reference's Triton path (child process, N=1 only)")
     ap.add_argument("--soft-only", action="store_true", help="profile the soft leg alone")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the hard batch (small cases for profiling)")
@@ -516,24 +737,45 @@ def main():
     ws, rank, local = dist_env()
     warmup = max(3, a.warmup)
     metric = "hard-circuit samples/s (bit-packed inference)"
-    cpu_n = a.cpu_sample or DEFAULT_CPU_SAMPLE[a.config]
+
+    if a.impl == "reference-gpu":
+        run_reference_gpu(a.config, cfg, a)
+        return
 
     if a.impl == "reference":
+        # the reference's own CPU path on the host cores, rank 0 only
         if rank != 0:
             return
-        threads = os.cpu_count() or 1
-        n = cpu_n * 4 if a.config in ("c1", "c2") else cpu_n
-        cpu_hard_sample(cfg, n, threads)
-        vals = [cpu_hard_sample(cfg, n, threads)[0] for _ in range(a.steps)]
-        v = statistics.mean(vals)
+        silogic = import_reference()
+        n = CPU_SAMPLE[a.config] // (4 if a.config == "c5" else 1)
+        x = make_input(cfg, n, seed=1)
+        if silogic is not None:
+            m, bp, enc = reference_net(silogic, cfg)
+            step = lambda: reference_cpu_step(silogic, cfg, bp, enc, x)
+            kind = "reference"
+            what = ("the reference's CPU path from baseline/_ref (input encoding + "
+                    "BitpackedNet/BitpackedConvNet, numpy)")
+        else:
+            step = lambda: cpu_port_sample(cfg, x)
+            kind, what = "port", "the numpy restatement of the reference (oracle/hard.py)"
+        for _ in range(warmup):
+            step()
+        ts = []
+        for _ in range(a.steps):
+            t0 = time.perf_counter()
+            step()
+            ts.append(time.perf_counter() - t0)
+        v = n / statistics.mean(ts)
+        threads = torch.get_num_threads()
         print(json.dumps({
             "metric": metric, "value": v, "unit": "samples/s", "n_gpus": ws, "steps": a.steps,
-            "warmup": warmup, "ms_per_step": n / v * 1e3, "higher_is_better": True,
+            "warmup": warmup, "ms_per_step": statistics.mean(ts) * 1e3, "higher_is_better": True,
             "impl": "reference", "dtype": "u64", "data": "synthetic",
-            "config": {"workload": cfg["name"], "batch": n},
-            "cpu_baseline": {"value": v, "unit": "samples/s", "cores": threads, "kind": "port",
-                             "sample": f"{n} samples per step through the numpy bit-packed "
-                                       f"restatement of the reference, {threads} threads"},
+            "config": {"workload": cfg["name"], "batch": n,
+                       "sample": f"{n} samples per step (bounded sample of the workload)"},
+            "cpu_baseline": {"value": v, "unit": "samples/s", "cores": threads, "kind": kind,
+                             "sample": f"{n} samples per step through {what}; torch threads "
+                                       f"{threads}, host cpus {os.cpu_count()}"},
             "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}))
         return
@@ -544,7 +786,6 @@ def main():
         torch.distributed.init_process_group("nccl")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    B = cfg["hard_batch"] // (ws if cfg["scaling"] == "strong" else 1)
     if a.soft_only:
         soft = run_soft(cfg, cfg["soft_batch"], a.steps, warmup, rank, ws, dev)
         if rank == 0:
@@ -552,60 +793,49 @@ def main():
                               "value": cfg["soft_batch"] * ws / (soft["ms"] * 1e-3),
                               "ms_per_step": soft["ms"]}))
         return
-    r = run_hard(cfg, B, a.steps, warmup, rank, ws, dev)
-    soft = None
-    if not a.no_soft and cfg["soft_batch"]:
-        soft = run_soft(cfg, cfg["soft_batch"], a.steps, warmup, rank, ws, dev)
-    ms = torch.tensor([r["ms"], r["e2e_ms"], soft["ms"] if soft else 0.0], device=dev)
-    if ws > 1:
-        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
-    ms_step, e2e_ms, soft_ms = ms.tolist()
-    hbm, kind = peaks()
+    res = measure_ours(a.config, cfg, a, ws, rank, dev, warmup, with_soft=not a.no_soft)
+    if a.extras is None:
+        extras = ["c2"] if (a.config == "c5" and not a.batch) else []
+    else:
+        extras = [e for e in a.extras.split(",") if e and e != "none"]
+    extra_res = {}
+    for e in extras:
+        torch.cuda.empty_cache()
+        extra_res[e] = measure_ours(e, dict(CONFIGS[e]), a, ws, rank, dev, warmup,
+                                    with_soft=not a.no_soft)
     if rank == 0:
-        # dominant kernel kind and its achieved bandwidth (algorithmic bytes / launch time)
-        dom = max(r["kern"], key=lambda k: r["kern"][k][0])
-        dom_ms, dom_n = r["kern"][dom]
-        dom_bytes = r["per_kind"][dom] * B
-        ach = dom_bytes / (dom_ms * 1e-3) / 1e9
-        total = B * ws if cfg["scaling"] == "weak" else cfg["hard_batch"]
         line = {
-            "metric": metric, "value": total / (ms_step * 1e-3), "unit": "samples/s", "n_gpus": ws,
-            "steps": a.steps, "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True,
-            "scaling": cfg["scaling"], "vs_baseline": None, "dtype": "u64",
-            "data": "synthetic (seeded inputs, N(0,1) parameters)",
-            "config": {"workload": cfg["name"], "batch_per_gpu": B, "global_batch": total,
+            "metric": metric, "value": res["value"], "unit": "samples/s", "n_gpus": ws,
+            "steps": a.steps, "warmup": warmup, "ms_per_step": res["ms_per_step"],
+            "higher_is_better": True, "scaling": cfg["scaling"], "vs_baseline": None,
+            "dtype": "u64", "data": "synthetic (seeded inputs, N(0,1) parameters)",
+            "config": {"workload": cfg["name"], "batch_per_gpu": res["B"],
+                       "global_batch": res["total"],
                        "parallelism": f"batch shard x{ws}, counts all-gathered",
                        "l2": "flushed before each step (256 MB write, then read back so L2 is clean)",
                        "launch": "one CUDA graph per chunk shape (pack + every layer + GroupSum)",
                        "clocks": "sampled over >= 1 s of untimed replays of the same step, then the timed steps"},
-            "e2e": {"value": total / (e2e_ms * 1e-3), "unit": "samples/s",
-                    "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
-            "gpu_launches": int(round(r["launches_per_step"] * a.steps)),
-            "roofline": {"kernel": f"slg_{dom} ({dom_n:.0f} launches/step)", "bound": "hbm",
-                         "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
-                         "peak_kind": kind,
-                         "traffic": NCU_TRAFFIC.get((a.config, dom), (None,))[0] if not a.batch else None,
-                         "traffic_source": NCU_TRAFFIC.get((a.config, dom), (None, None))[1],
-                         "algorithmic_bytes_per_step": dom_bytes,
-                         "step_frac": r["bytes_per_sample"] * B / (ms_step * 1e-3) / 1e9 / hbm},
-            "kernels_ms_per_step": {k: v[0] for k, v in r["kern"].items()},
-            "clocks": r["clocks"],
+            "e2e": res["e2e"], "gpu_launches": res["gpu_launches"], "roofline": res["roofline"],
+            "kernels_ms_per_step": res["kernels_ms_per_step"], "clocks": res["clocks"],
+            "parity": res.get("parity"),
         }
-        if soft:
-            Bs = cfg["soft_batch"]
-            ach_s = soft["bytes_per_sample"] * Bs / (soft_ms * 1e-3) / 1e9
-            line["soft_fwd_bwd"] = {
-                "metric": "soft fwd+bwd samples/s", "value": Bs * ws / (soft_ms * 1e-3),
-                "unit": "samples/s", "ms_per_step": soft_ms, "batch_per_gpu": Bs, "dtype": "f32",
-                "roofline": {"bound": "hbm (layer-wise bytes; gathers are L2-bound)",
-                             "achieved": ach_s, "peak": hbm, "unit": "GB/s", "frac": ach_s / hbm,
-                             "algorithmic_bytes_per_sample": soft["bytes_per_sample"]},
-                "collective": "one NCCL all-reduce of all parameter gradients" if ws > 1 else None}
-        if ws == 1:
-            v, dt = cpu_hard_sample(cfg, cpu_n, 1)
-            line["cpu_baseline"] = {"value": v, "unit": "samples/s", "cores": 1, "kind": "port",
-                                    "sample": f"{cpu_n} samples through the numpy bit-packed "
-                                              f"restatement of the reference ({dt:.2f} s)"}
+        if "soft_fwd_bwd" in res:
+            line["soft_fwd_bwd"] = res["soft_fwd_bwd"]
+        for e, er in extra_res.items():
+            line[e] = {k: er[k] for k in ("value", "ms_per_step", "e2e", "roofline", "parity",
+                                          "kernels_ms_per_step", "soft_fwd_bwd") if k in er}
+            line[e].update(workload=CONFIGS[e]["name"], batch_per_gpu=er["B"],
+                           scaling=CONFIGS[e]["scaling"], unit="samples/s")
+        if ws == 1 and not a.no_cpu:
+            r = res["r"]
+            line["cpu_baseline"] = cpu_baseline(a.config, cfg, r["x_first"], r["counts_first"])
+            for e, er in extra_res.items():
+                line[e]["cpu_baseline"] = cpu_baseline(e, CONFIGS[e], er["r"]["x_first"],
+                                                       er["r"]["counts_first"])
+        if ws == 1 and a.reference_gpu:
+            del res, extra_res
+            torch.cuda.empty_cache()
+            line["reference_gpu"] = reference_gpu(a.config, 16384 if a.config == "c5" else 65536)
         print(json.dumps(line))
     if ws > 1:
         torch.distributed.destroy_process_group()

@@ -73,6 +73,18 @@ int slg_thermo_pack(const float* x, int64_t B, int64_t C, int64_t HW, const floa
 
 /* ----------------------------------------------------------- hard circuit */
 
+/* Validate gather indices before they reach a kernel: every idx[i] (i < count) must
+ * lie in [0, limit).  The kernels of this library trust their wiring (an index out of
+ * range is an out-of-bounds device read), so hosts check each wiring array once when
+ * they build or load a circuit -- FC wiring against the layer's input width, conv
+ * leaves against cin*kernel*kernel, soft candidates against the input width.
+ * `scratch` is 16 bytes of caller device memory (8-byte aligned).  Synchronises
+ * `stream`; returns SLG_ERR_ARG naming the first bad position and value.  Replaces the
+ * reference's implicit Python indexing errors (silogic/bitpacking/packed_layer.py:85-116
+ * raises IndexError on a bad wiring index; its Triton kernels do not check). */
+int slg_check_index_range(const int32_t* idx, int64_t count, int64_t limit, void* scratch,
+                          void* stream);
+
 /* One FC logic layer on packed activations:
  *   out[o] = LUT_o(x[idx[o*arity + 0]], ..., x[idx[o*arity + arity-1]])   (o >= wire_r)
  *   out[o] = x[o]                                                         (o <  wire_r)
@@ -200,10 +212,14 @@ int slg_fc_soft_bwd(const float* x, int64_t in_dim, int64_t ldb, const int32_t* 
  * or a latency-critical loop that must never enter the allocator).  It has no
  * counterpart in the reference.  Its scratch is a static device array of
  * SLG_FC_NOALLOC_SCRATCH_BYTES per GPU, resident until process exit; sizes whose
- * slg_fc_soft_workspace_bytes exceed it fail with SLG_ERR_WORKSPACE.  The first
- * call on a device looks up the array's address (make it before any stream
- * capture).  All calls on a device share the array: calls that overlap on the
- * GPU race.  Same arguments and results as slg_fc_soft_bwd otherwise. */
+ * slg_fc_soft_workspace_bytes exceed it fail with SLG_ERR_WORKSPACE.  Scalar
+ * arguments are checked first (same codes as slg_fc_soft_bwd), then the scratch
+ * size, then the pointers, so NULL pointers answer the size question.  The first
+ * call on a device looks up the array's address and caches it for the life of the
+ * process (make it before any stream capture; the cache assumes the device is never
+ * reset with cudaDeviceReset).  All calls on a device share the array: calls that
+ * overlap on the GPU race.  Same arguments and results as slg_fc_soft_bwd
+ * otherwise. */
 #define SLG_FC_NOALLOC_SCRATCH_BYTES (16ll << 20)
 int slg_fc_soft_bwd_noalloc(const float* x, int64_t in_dim, int64_t ldb, const int32_t* cand,
                             const float* conn, int32_t K, int32_t conn_ste, int32_t node,

@@ -86,22 +86,38 @@ def node_truth_tables(node, params, arity, mono_mask=None):
     if node in ("multilinear", "hybrid"):
         return params > 0                                     # nodes.py:188
     if node == "walsh":
-        # z = sum_M theta_M prod_{j in M} (2 bit_j - 1) > 0   (nodes.py:153-156)
-        u = 2 * cb - 1                                        # [P, n]
-        mono = np.ones((P, P))
+        # z = sum_M theta_M prod_{j in M} (2 bit_j - 1) > 0 in fp32, monomials added in
+        # index order as the reference's forward_hard sums them (nodes.py:153-156;
+        # walsh_monomials column order, functional.py:176-185); the arity-2 bit-packed
+        # conversion (convert.py:84-97) adds the same fp32 terms in the same order.
+        u = (2 * cb - 1).astype(np.float32)                   # [P, n]
+        mono = np.ones((P, P), dtype=np.float32)
         for m in range(P):
             for j in range(arity):
                 if (m >> j) & 1:
                     mono[:, m] *= u[:, j]
-        z = params.astype(np.float64) @ mono.T                # [out, P]
+        th = params.astype(np.float32)
+        z = np.zeros((th.shape[0], P), dtype=np.float32)
+        for m in range(P):
+            z = z + th[:, m:m + 1] * mono[None, :, m]
         return z > 0
     if node == "linear":
-        z = params[:, :1].astype(np.float64) + params[:, 1:].astype(np.float64) @ cb.T
-        return z >= 0                                         # nodes.py:232-233
+        # fp32: bias + sum_j theta_j a_j, inputs added in slot order (nodes.py:225-233)
+        th = params.astype(np.float32)
+        cbf = cb.astype(np.float32)
+        z = np.repeat(th[:, :1], P, axis=1)
+        for j in range(arity):
+            z = z + th[:, 1 + j:2 + j] * cbf[None, :, j]
+        return z >= 0
     if node == "polynomial":
-        mk = np.asarray(mono_mask, dtype=np.float64)          # [M, n]
-        mono = np.prod(np.where(mk[None] > 0, cb[:, None, :], 1), axis=2)  # [P, M]
-        return params.astype(np.float64) @ mono.T >= 0
+        # fp32 sum over the monomials in mask-row order (nodes.py:256-268)
+        mk = np.asarray(mono_mask, dtype=np.float32)          # [M, n]
+        mono = np.prod(np.where(mk[None] > 0, cb[:, None, :], 1), axis=2).astype(np.float32)
+        th = params.astype(np.float32)
+        z = np.zeros((th.shape[0], P), dtype=np.float32)
+        for m in range(mono.shape[1]):
+            z = z + th[:, m:m + 1] * mono[None, :, m]
+        return z >= 0
     raise ValueError(node)
 
 

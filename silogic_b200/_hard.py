@@ -5,11 +5,12 @@ with ``ldw = ceil(B/64)`` rounded up to even; sample ``b`` is bit ``b % 64`` of
 word ``b // 64``, as in ``silogic/bitpacking/ops.py:32-49``.
 """
 import ctypes
+import weakref
 
 import torch
 
 from . import _lib
-from ._lib import call, ptr, require_cuda, stream_ptr
+from ._lib import call, lib, ptr, require_cuda, stream_ptr
 from .functional import gate16_lut_codes
 
 _GATE_LUT = gate16_lut_codes()
@@ -97,6 +98,44 @@ def thermo_pack(img, thresholds, mode=0, ldw=None):
     call("slg_thermo_pack", ptr(x), B, C, H * W, ptr(thr), T, mode, ptr(out), ldw,
          stream_ptr(img.device))
     return out
+
+
+# ----------------------------------------------------------- wiring checks
+_CHECKED = weakref.WeakKeyDictionary()   # index tensor -> (version, limit) that passed
+
+
+def check_index_range(idx, limit, what="index"):
+    """Raise ``IndexError`` unless every entry of ``idx`` lies in ``[0, limit)``.
+
+    The kernels trust their wiring (an index out of range is an out-of-bounds device
+    read), so every circuit is checked once when it is built or loaded: FC wiring
+    against the layer's input width, conv leaves against ``cin * k * k``, soft
+    candidates against the input width.  CUDA tensors go through the library's
+    ``slg_check_index_range`` (one small kernel + a synchronisation); host tensors are
+    checked on the host.  A tensor that passed is remembered until it is modified
+    in place (its version counter changes).
+    """
+    if idx is None or idx.numel() == 0:
+        return
+    seen = _CHECKED.get(idx)
+    if seen is not None and seen[0] == idx._version and seen[1] <= limit:
+        return
+    if idx.is_cuda:
+        i32 = idx if idx.dtype == torch.int32 else idx.to(torch.int32)
+        if idx.dtype != torch.int32 and (idx.min() < -2**31 or idx.max() >= 2**31):
+            raise IndexError(f"{what}: entries do not fit in int32")
+        i32 = i32.contiguous()
+        scratch = torch.empty(2, dtype=torch.int64, device=idx.device)
+        st = lib().slg_check_index_range(ptr(i32), i32.numel(), int(limit), ptr(scratch),
+                                         stream_ptr(idx.device))
+        if st != 0:
+            raise IndexError(f"{what}: " + lib().slg_last_error().decode(errors="replace"))
+    else:
+        lo, hi = int(idx.min()), int(idx.max())
+        if lo < 0 or hi >= limit:
+            raise IndexError(f"{what}: index out of range: entries span [{lo}, {hi}], "
+                             f"allowed [0, {limit})")
+    _CHECKED[idx] = (idx._version, int(limit))
 
 
 # ---------------------------------------------------------------- circuits

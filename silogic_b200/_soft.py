@@ -85,6 +85,7 @@ def _fc_meta(layer, wire_r=0):
     inv_tau = float(node.inv_tau) if kind == "walsh" else 1.0
     if kind == "polynomial":    # same function in the Walsh basis (see PolynomialNode)
         params, kind = node.walsh_theta(), "walsh"
+    _hard.check_index_range(cand, layer.in_dim, "LogicLayer candidates")
     return dict(cand=cand.contiguous(), K=K, ste=ste, node=NODE_ID[kind], arity=layer.arity,
                 gate_hard=gate_hard, inv_tau=inv_tau, out_dim=layer.out_dim,
                 wire_r=wire_r), params, conn
@@ -215,6 +216,7 @@ def _conv_meta(conv, wire_r=0, pool=1):
         conn, K, ste = conv.conn, conv.k, int(conv.gate_select == "hard")
     if K > 16:
         raise NotImplementedError("soft conv kernels support at most 16 candidates per leaf")
+    _hard.check_index_range(cand, conv.cin * conv.kh * conv.kw, "ConvLogicTree leaf candidates")
     levels = conv.level_params()
     if kind == "gate16":
         params = torch.cat(list(levels), dim=1)                        # [n, nodes, 16]

@@ -50,10 +50,17 @@ class PackedFCLayer:
         self.idx = idx.to(torch.int32).contiguous()
         self.tt = tt.to(torch.int64).contiguous()
         self.out_dim, self.arity = self.idx.shape
+        # the input width this wiring needs (checked once here: no index may be
+        # negative; forward checks the input has more rows than the largest index)
+        _hard.check_index_range(self.idx, 2**31 - 1, "FC wiring")
+        self.min_in_dim = int(self.idx.max()) + 1 if self.idx.numel() else 0
 
     def forward(self, x):
         """``[in, n_words]`` int64 (numpy or CUDA) -> ``[out, n_words]``."""
         t, nw, was_np = _packed_in(x, self.idx.device)
+        if t.shape[0] < self.min_in_dim:
+            raise IndexError(f"FC wiring reads input row {self.min_in_dim - 1} but the input "
+                             f"has {t.shape[0]} rows")
         return _packed_out(_hard.fc(t, self.idx, self.tt), nw, was_np)
 
     __call__ = forward
@@ -85,9 +92,12 @@ class PackedConvLayer:
         self.arity, self.depth, self.kh, self.kw = arity, depth, kernel, kernel
         self.padding, self.stride, self.cin, self.n_out = pad, 1, cin, n
         self.n_leaves = leaf.shape[1]
+        _hard.check_index_range(self.leaf, cin * kernel * kernel, "conv leaf taps")
 
     def forward(self, x4, pool=2, wire_r=0):
         """Packed ``[C, H, W, ldw]`` CUDA -> ``[n, Ho/pool, Wo/pool, ldw]``."""
+        if x4.shape[0] != self.cin:
+            raise ValueError(f"conv layer built for {self.cin} input channels, got {x4.shape[0]}")
         return _hard.conv(x4, self.leaf, self.tt, self.arity, self.depth, self.kh,
                           self.padding, wire_r, pool)
 
@@ -96,6 +106,9 @@ class PackedConvLayer:
         the taps become 1x1 taps over ``P`` channels."""
         t, nw, was_np = _packed_in(x_3d, self.leaf.device)
         P, L, ldw = t.shape
+        if P != self.cin * self.kh * self.kw:
+            raise ValueError(f"unfolded input must have cin*k*k = {self.cin * self.kh * self.kw} "
+                             f"rows, got {P}")
         y = _hard.conv(t.view(P, L, 1, ldw), self.leaf, self.tt, self.arity, self.depth,
                        kernel=1, pad=0, wire_r=0, pool=1)
         return _packed_out(y.view(self.n_out, L, ldw), nw, was_np)

@@ -40,6 +40,22 @@ def _order_channels_for_locality(steps):
             nxt["idx"] = (inv[idx // hw] * hw + idx % hw).to(nxt["idx"].dtype).contiguous()
 
 
+def validate_steps(steps, width):
+    """Check every gather index of a plan against the width it reads (once, at build):
+    FC wiring < the layer's input width, conv leaves < cin * k * k.  ``width`` is the
+    input feature count (FC) or input channel count (conv)."""
+    for i, st in enumerate(steps):
+        if st["op"] == "conv":
+            kk = st["kernel"] * st["kernel"]
+            _hard.check_index_range(st["leaf"], width * kk, f"conv block {i} leaf taps")
+            width = st["n"]
+        else:
+            if "in_dim" in st:
+                width = st["in_dim"]
+            _hard.check_index_range(st["idx"], width, f"FC layer {i} wiring")
+            width = st["idx"].shape[0]
+
+
 class HardPlan:
     """Wiring + truth tables of every layer, on the parameters' device."""
 
@@ -82,6 +98,7 @@ class HardPlan:
                 wr = model.wire_r if (model.wire_r and layer.in_dim == layer.out_dim) else 0
                 steps.append(dict(op="fc", idx=idx, tt=tt, wire_r=wr))
             in_shape = ("fc", d_in)
+            validate_steps(steps, d_in)
         elif isinstance(model, LogicConvNet):
             convs = [b for b in model.blocks[0::2]]
             pools = [b for b in model.blocks[1::2]]
@@ -96,6 +113,7 @@ class HardPlan:
                 idx, tt = layer.hard_spec()
                 steps.append(dict(op="fc", idx=idx, tt=tt, wire_r=0, in_dim=layer.in_dim))
             in_shape = ("conv", first.cin, None, None)
+            validate_steps(steps, first.cin)
             if LOCALITY_ORDER and all(st["wire_r"] == 0 for st in steps):
                 _order_channels_for_locality(steps)
         else:
@@ -109,6 +127,13 @@ class HardPlan:
     def pack_input(self, x):
         """Pack a binary input batch (``[B, F]`` or ``[B, C, H, W]``)."""
         B = x.shape[0]
+        want = self.in_shape[1]
+        got = x.shape[1] if x.dim() == 4 else x.reshape(B, -1).shape[1]
+        if x.dim() == 4 and self.in_shape[0] == "fc":
+            got = x[0].numel()
+        if got != want:
+            raise ValueError(f"the circuit expects {want} input "
+                             f"{'features' if self.in_shape[0] == 'fc' else 'channels'}, got {got}")
         h = _hard.pack(x.reshape(B, -1))
         if x.dim() == 4:
             h = h.view(x.shape[1], x.shape[2], x.shape[3], -1)
@@ -177,6 +202,9 @@ class HardGraph:
             h = self.plan.pack_input(self.x)
         else:
             h = _hard.thermo_pack(self.x, self.thresholds, mode=self.mode)
+            if self.plan.in_shape[0] == "conv" and h.shape[0] != self.plan.in_shape[1]:
+                raise ValueError(f"thermometer encoding gives {h.shape[0]} channels, the "
+                                 f"circuit expects {self.plan.in_shape[1]}")
         if self.head is not None:
             return None, self.head.apply(self.plan.run_packed(h), B)
         counts = self.plan.counts_from_packed(h, B, out=self._out)

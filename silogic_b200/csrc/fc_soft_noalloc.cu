@@ -11,9 +11,15 @@
 //    on every GPU that loads the library until the process exits.
 //  * Sizes whose scratch (slg_fc_soft_workspace_bytes) exceeds it are rejected
 //    with SLG_ERR_WORKSPACE; nothing is allocated, ever.
+//  * Arguments are checked in this order: the scalar arguments (sizes, K, ldb,
+//    node, arity) with the status codes slg_fc_soft_bwd returns for them, then the
+//    scratch size (SLG_ERR_WORKSPACE), then the pointers.  A call with NULL
+//    pointers therefore answers the size question without any buffer.
 //  * The first call on a device resolves the array's device address
-//    (cudaGetSymbolAddress with that device current) and caches it; make that
-//    first call before any stream capture.
+//    (cudaGetSymbolAddress with that device current) and caches it for the life of
+//    the process; make that first call before any stream capture.  The cache
+//    assumes the device's context is never torn down: after cudaDeviceReset the
+//    cached address is stale, so do not reset a device this entry point has used.
 //  * Every call on a device shares the one array and leaves the last call's
 //    partials in it.  The kernels overwrite every scratch entry they later read,
 //    so nothing needs clearing between calls, but calls whose execution overlaps
@@ -59,6 +65,13 @@ extern "C" int slg_fc_soft_bwd_noalloc(const float* x, int64_t in_dim, int64_t l
                                        int32_t arity, const float* params, int32_t gate_hard, float inv_tau,
                                        int64_t out_dim, int64_t wire_r, const float* gy, float* gx,
                                        float* gconn, float* gparams, void* stream) {
+    // scalar arguments first, with the codes slg_fc_soft_bwd gives them
+    if (in_dim <= 0 || out_dim < 0 || ldb <= 0 || K <= 0 || wire_r < 0)
+        return set_error(SLG_ERR_ARG, "slg_fc_soft_bwd_noalloc: bad sizes");
+    if (K > FS_KMAX) return set_error(SLG_ERR_UNSUPPORTED, "slg_fc_soft_bwd_noalloc: K=%d > %d", K, FS_KMAX);
+    if (ldb % 4) return set_error(SLG_ERR_ALIGN, "slg_fc_soft_bwd_noalloc: ldb must be a multiple of 4");
+    if (node < N_GATE16 || node > N_LINEAR || arity < 1 || arity > 6 || (node == N_GATE16 && arity != 2))
+        return set_error(SLG_ERR_ARG, "slg_fc_soft_bwd_noalloc: node %d arity %d", node, arity);
     const int64_t need = slg_fc_soft_workspace_bytes(ldb, K, node, arity, out_dim);
     if (need > kNoallocScratchBytes)
         return set_error(SLG_ERR_WORKSPACE,

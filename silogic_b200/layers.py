@@ -82,7 +82,11 @@ class LogicLayer(nn.Module):
     @torch.no_grad()
     def forward_hard(self, x):
         B = x.shape[0]
+        if x.reshape(B, -1).shape[1] != self.in_dim:
+            raise ValueError(f"LogicLayer expects {self.in_dim} input features, got "
+                             f"{x.reshape(B, -1).shape[1]}")
         idx, tt = self.hard_spec()
+        _hard.check_index_range(idx, self.in_dim, "LogicLayer wiring")
         return _hard.unpack(_hard.fc(_hard.pack(x), idx, tt), B)
 
 
@@ -291,7 +295,10 @@ class ConvLogicTree(nn.Module):
     @torch.no_grad()
     def forward_hard(self, x):
         B, C, H, W = x.shape
+        if C != self.cin:
+            raise ValueError(f"ConvLogicTree expects {self.cin} input channels, got {C}")
         leaf, tt = self.hard_spec()
+        _hard.check_index_range(leaf, self.cin * self.kh * self.kw, "ConvLogicTree leaf taps")
         h = _hard.pack(x.reshape(B, -1)).view(C, H, W, -1)
         y = _hard.conv(h, leaf, tt, self.node_arity, self.d, self.kh, self.padding, pool=1)
         Ho, Wo = self._hw_out(H, W)

@@ -92,3 +92,39 @@ def test_chain_planner_runs_on_the_host_and_rejects_bad_wiring():
     bad[3, 1] = in_dim                 # one past the input layer
     assert plan(bad, 1) != 0
     assert b"out of range" in _lib.lib().slg_last_error()
+
+
+def test_index_check_rejects_null_and_bad_sizes(L):
+    """slg_check_index_range validates its arguments before touching any memory."""
+    assert L.slg_check_index_range(None, 0, 10, None, None) == 0          # nothing to check
+    assert L.slg_check_index_range(None, 5, 10, None, None) == 1
+    assert L.slg_check_index_range(None, -1, 10, None, None) == 1
+
+
+def test_plan_and_layers_reject_out_of_range_wiring():
+    """A wiring index outside the layer's input (e.g. from a corrupted checkpoint) is
+    refused when the circuit is built, before any kernel could read past the input."""
+    import torch
+    import silogic_b200 as S
+    from silogic_b200.bitpacking.plan import HardPlan
+    from silogic_b200.bitpacking.packed import PackedFCLayer, PackedConvLayer
+    torch.manual_seed(0)
+    m = S.LogicNet(20, 30, 2, node="gate16", connectome="topk", k=4, tau=1.0, seed=0)
+    HardPlan.from_model(m)                                           # valid wiring builds
+    with torch.no_grad():
+        m.layers[1]._conn.cand[0, 0, :] = 30                         # layer 1 reads 30 rows
+    with pytest.raises(IndexError, match="FC layer 1"):
+        HardPlan.from_model(m)
+    with pytest.raises(IndexError):
+        PackedFCLayer(torch.tensor([[0, -1]], dtype=torch.int32), torch.tensor([6]))
+    conv = S.LogicTreeNet(in_channels=3, in_hw=8, channels=[4, 8], head_widths=[40], tree_depth=1,
+                          node="gate16", tau=1.0, seed=0)
+    HardPlan.from_model(conv)
+    with torch.no_grad():
+        blk = conv.blocks[2]
+        (blk.leaf_cand if blk.connect != "fixed" else blk.leaf_idx)[0, 0] = 4 * 9   # cin*k*k
+    with pytest.raises(IndexError, match="conv block 1"):
+        HardPlan.from_model(conv)
+    with pytest.raises(IndexError):
+        PackedConvLayer(torch.tensor([[0, 27]], dtype=torch.int32), torch.tensor([[6]]), 2, 1, 3,
+                        1, 3, 1)

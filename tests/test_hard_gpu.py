@@ -345,3 +345,22 @@ def test_learned_decoder_bitpacked_head(decoder):
             np.testing.assert_array_equal(got, ref)
         else:
             np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-4)
+
+
+def test_device_index_check_names_the_first_bad_entry():
+    """slg_check_index_range on device wiring: in-range passes, one bad entry is refused
+    with its position and value, and a circuit built from it never launches."""
+    from silogic_b200 import _hard
+    idx = torch.randint(0, 100, (5000, 2), dtype=torch.int32, device=dev)
+    _hard.check_index_range(idx, 100, "wiring")
+    bad = idx.clone()
+    bad[1234, 1] = 100
+    bad[4000, 0] = -3
+    with pytest.raises(IndexError, match=r"2 of 10000 entries outside \[0, 100\), first at "
+                                         r"position 2469 \(value 100\)"):
+        _hard.check_index_range(bad, 100, "wiring")
+    from silogic_b200.bitpacking.packed import PackedFCLayer
+    layer = PackedFCLayer(idx, torch.zeros(5000, dtype=torch.int64, device=dev))
+    x = torch.zeros(50, 2, dtype=torch.int64, device=dev)            # only 50 input rows
+    with pytest.raises(IndexError, match="reads input row"):
+        layer(x)
