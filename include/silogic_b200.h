@@ -85,6 +85,15 @@ int slg_thermo_pack(const float* x, int64_t B, int64_t C, int64_t HW, const floa
 int slg_check_index_range(const int32_t* idx, int64_t count, int64_t limit, void* scratch,
                           void* stream);
 
+/* Process-wide tuning knobs (thread-safe; the defaults are the measured best):
+ *   key 0  arity-2 conv trees use the uniform gate-dispatch kernel (1) or the
+ *          generic LUT-tree kernel (0); both give identical bits;
+ *   key 1  pooled positions per thread in that kernel (8);
+ *   key 2  sorted near-uniform thermometer thresholds use the grid guess with two
+ *          corrective comparisons (1) or a binary search (0); both give identical bits.
+ * No counterpart in the reference (its Triton kernels take fixed block sizes). */
+int slg_tuning_set(int32_t key, int64_t value);
+
 /* One FC logic layer on packed activations:
  *   out[o] = LUT_o(x[idx[o*arity + 0]], ..., x[idx[o*arity + arity-1]])   (o >= wire_r)
  *   out[o] = x[o]                                                         (o <  wire_r)

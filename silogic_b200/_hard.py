@@ -101,7 +101,7 @@ def thermo_pack(img, thresholds, mode=0, ldw=None):
 
 
 # ----------------------------------------------------------- wiring checks
-_CHECKED = weakref.WeakKeyDictionary()   # index tensor -> (version, limit) that passed
+_CHECKED = {}   # id(index tensor) -> (weakref to it, version, limit) that passed
 
 
 def check_index_range(idx, limit, what="index"):
@@ -117,8 +117,10 @@ def check_index_range(idx, limit, what="index"):
     """
     if idx is None or idx.numel() == 0:
         return
-    seen = _CHECKED.get(idx)
-    if seen is not None and seen[0] == idx._version and seen[1] <= limit:
+    if torch.compiler.is_compiling():      # host validation; the eager call checked it
+        return
+    seen = _CHECKED.get(id(idx))
+    if seen is not None and seen[0]() is idx and seen[1] == idx._version and seen[2] <= limit:
         return
     if idx.is_cuda:
         i32 = idx if idx.dtype == torch.int32 else idx.to(torch.int32)
@@ -135,7 +137,10 @@ def check_index_range(idx, limit, what="index"):
         if lo < 0 or hi >= limit:
             raise IndexError(f"{what}: index out of range: entries span [{lo}, {hi}], "
                              f"allowed [0, {limit})")
-    _CHECKED[idx] = (idx._version, int(limit))
+    if len(_CHECKED) > 4096:
+        for k in [k for k, v in _CHECKED.items() if v[0]() is None]:
+            del _CHECKED[k]
+    _CHECKED[id(idx)] = (weakref.ref(idx), idx._version, int(limit))
 
 
 # ---------------------------------------------------------------- circuits

@@ -22,6 +22,7 @@ _f32 = ctypes.c_float
 _SIGS = {
     "slg_version": [],
     "slg_check_index_range": [_p, _i64, _i64, _p, _p],
+    "slg_tuning_set": [_i32, _i64],
     "slg_pack_u8": [_p, _i64, _i64, _p, _i64, _p],
     "slg_pack_f32": [_p, _i64, _i64, _p, _i64, _p],
     "slg_unpack_u8": [_p, _i64, _i64, _i64, _p, _p],

@@ -140,7 +140,7 @@ def node_forward(node, x, idx):
     torch.nn.Module.__init__(conn)
     conn.cand_i32 = idx.unsqueeze(-1).contiguous()
     fake = SimpleNamespace(node=node, _conn=conn, arity=node.arity, out_dim=node.out_dim,
-                           training=node.training)
+                           in_dim=x.reshape(x.shape[0], -1).shape[1], training=node.training)
     meta, params, c = _fc_meta(fake)
     B = x.shape[0]
     return FromFeatureMajor.apply(FCSoft.apply(ToFeatureMajor.apply(x), params, c, meta), B)

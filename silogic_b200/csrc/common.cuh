@@ -21,6 +21,16 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Process-wide tuning knobs (slg_tuning_set); defaults are the measured best.
+enum TuningKey { T_CONV_GATE2 = 0, T_CONV_PPT = 1, T_THERMO_GUESS = 2, T_NUM_KEYS = 3 };
+int64_t tuning(int key);
+
+// Arity-2 conv tree blocks with uniform gate dispatch (conv_gate2.cu); false when the
+// shape is not one it handles (the caller then uses the generic LUT tree kernel).
+bool launch_conv_gate2(const uint4* x, int64_t cin, int H, int W, int nvec, const int32_t* leaf,
+                       const uint64_t* tt, int depth, int kernel, int pad, int64_t n_out,
+                       int64_t wire_r, int pool, int Hp, int Wp, uint4* out, cudaStream_t st);
+
 __host__ __device__ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // All-ones / zero 32-bit mask from bit p of a 64-bit truth table.

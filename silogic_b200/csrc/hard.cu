@@ -449,6 +449,12 @@ extern "C" int slg_conv_hard(const uint64_t* x, int64_t cin, int64_t H, int64_t 
     const int64_t nvec = ldw / 2;
     if (H * W * nvec >= (1ll << 31) || Hp * Wp * nvec >= (1ll << 31))
         return set_error(SLG_ERR_UNSUPPORTED, "slg_conv_hard: channel plane over 2^31 words; split the batch");
+    auto xs = reinterpret_cast<const uint4*>(x);
+    auto os = reinterpret_cast<uint4*>(out);
+    cudaStream_t st = as_stream(stream);
+    if (arity == 2 && launch_conv_gate2(xs, cin, (int)H, (int)W, (int)nvec, leaf, tt, depth, kernel, pad,
+                                        n_out, wire_r, pool, (int)Hp, (int)Wp, os, st))
+        return check_launch("slg_conv_hard");
     const int vt = pick_vt(nvec);
     int vs = 0;
     while ((1 << vs) < vt) ++vs;
@@ -462,9 +468,6 @@ extern "C" int slg_conv_hard(const uint64_t* x, int64_t cin, int64_t H, int64_t 
     if (gy > 65535 || n_out * tiles > 0x7fffffffLL || H * W > (1 << 24))
         return set_error(SLG_ERR_ARG, "slg_conv_hard: grid too large");
     dim3 grid((unsigned)(n_out * tiles), (unsigned)gy);
-    auto xs = reinterpret_cast<const uint4*>(x);
-    auto os = reinterpret_cast<uint4*>(out);
-    cudaStream_t st = as_stream(stream);
     const int key = arity * 10 + depth;
 #define SLG_CONV_CASE(A, D) \
     case A * 10 + D: launch_conv<A, D>(grid, st, xs, cin, (int)H, (int)W, (int)nvec, leaf, tt, kernel, pad, n_out, wire_r, pool, (int)Hp, (int)Wp, os, vs, (int)ppt); break;

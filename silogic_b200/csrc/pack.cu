@@ -172,10 +172,11 @@ template <int LOG>
 __global__ void __launch_bounds__(256)
 thermo_kernel(const float* __restrict__ x, int64_t B, int64_t C, int64_t HW,
               const float* __restrict__ thr, int T, int mode,
-              uint64_t* __restrict__ out, int64_t ldw) {
+              uint64_t* __restrict__ out, int64_t ldw, int use_guess) {
     __shared__ float tile[TH_S][TH_FT + 1];
     __shared__ float sthr[TH_FT][33];      // mode 0: row 0 only; mode 1: per feature
     __shared__ float s_srt[64];            // sorted chunk, padded with +inf
+    __shared__ float s_pad[34];            // NaN, the sorted chunk, NaN (guess-and-correct)
     __shared__ int64_t s_row[TH_FT];       // pixel p of each feature
     __shared__ int32_t s_c[TH_FT];         // channel c of each feature
     const int64_t F = C * HW;
@@ -226,6 +227,9 @@ thermo_kernel(const float* __restrict__ x, int64_t B, int64_t C, int64_t HW,
         if (mode == 0) {
             if (threadIdx.x < 32) sthr[0][threadIdx.x] = threadIdx.x < nt ? thr[t0 + threadIdx.x] : 0.0f;
             if (threadIdx.x < 64) s_srt[threadIdx.x] = threadIdx.x < nt ? thr[t0 + threadIdx.x] : __int_as_float(0x7f800000);
+            if (threadIdx.x < 34)
+                s_pad[threadIdx.x] = (threadIdx.x >= 1 && threadIdx.x <= nt) ? thr[t0 + threadIdx.x - 1]
+                                                                            : __int_as_float(0x7fc00000);
         } else {
             for (int i = threadIdx.x; i < TH_FT * nt; i += 256) {
                 const int f = i / nt, t = i % nt;
@@ -233,6 +237,24 @@ thermo_kernel(const float* __restrict__ x, int64_t B, int64_t C, int64_t HW,
             }
         }
         __syncthreads();
+        // Sorted shared thresholds that lie within a quarter of their mean spacing of a
+        // uniform grid: each value's count (thresholds <= v) is within one of the grid
+        // guess floor((v - t_0) / step) + 1, so the guess corrected by two independent
+        // comparisons is exact -- no dependent chain of shared-memory loads.
+        float u0 = 0.f, inv = 0.f;
+        bool uni = false;
+        if (LOG > 0) {
+            u0 = s_srt[0];
+            const float step = nt > 1 ? (s_srt[nt - 1] - u0) / (float)(nt - 1) : 0.f;
+            inv = 1.0f / step;
+            bool ok = use_guess && nt > 1 && step > 0.f && isfinite(step) && isfinite(inv);
+            if (ok && threadIdx.x < nt) {
+                const float tv = s_srt[threadIdx.x];
+                ok = fabsf(tv - (u0 + (float)threadIdx.x * step)) <= 0.25f * step &&
+                     (threadIdx.x == 0 || s_srt[threadIdx.x - 1] <= tv);
+            }
+            uni = __syncthreads_and(ok) != 0;
+        }
         for (int item = warp; item < ngroups * 2; item += 8) {
             const int g = item >> 1, wp = item & 1;       // feature group, word pair
             const int fa = g * grp;
@@ -246,7 +268,12 @@ thermo_kernel(const float* __restrict__ x, int64_t B, int64_t C, int64_t HW,
 #pragma unroll
                 for (int h = 0; h < 4; ++h) {
                     uint32_t m = 0;
-                    if (LOG > 0) {
+                    if (LOG > 0 && uni) {
+                        const float q = (v[h] - u0) * inv;
+                        const int g = q >= 0.f ? min((int)fminf(q, 64.f) + 1, nt) : 0;
+                        const int pos = g + (int)(v[h] >= s_pad[g + 1]) - (int)(v[h] < s_pad[g]);
+                        m = ((pos >= 32 ? 0xffffffffu : ((1u << pos) - 1u))) & tmask;
+                    } else if (LOG > 0) {
                         int pos = 0;
 #pragma unroll
                         for (int st = LOG - 1; st >= 0; --st) {
@@ -347,20 +374,21 @@ extern "C" int slg_thermo_pack(const float* x, int64_t B, int64_t C, int64_t HW,
     // mode 2 = mode 0 with thresholds the caller guarantees sorted ascending: binary
     // search in ceil(log2(nt + 1)) steps, nt = thresholds per 32-chunk
     cudaStream_t st = as_stream(stream);
+    const int guess = (int)tuning(T_THERMO_GUESS);
     if (mode == 2) {
         const int nt = (int)std::min<int64_t>(T, 32);
         int lg = 0;
         while ((1 << lg) < nt + 1) ++lg;       // 2^lg - 1 >= nt
         switch (lg) {
-            case 1: thermo_kernel<1><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw); break;
-            case 2: thermo_kernel<2><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw); break;
-            case 3: thermo_kernel<3><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw); break;
-            case 4: thermo_kernel<4><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw); break;
-            case 5: thermo_kernel<5><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw); break;
-            default: thermo_kernel<6><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw); break;
+            case 1: thermo_kernel<1><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
+            case 2: thermo_kernel<2><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
+            case 3: thermo_kernel<3><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
+            case 4: thermo_kernel<4><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
+            case 5: thermo_kernel<5><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
+            default: thermo_kernel<6><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
         }
     } else {
-        thermo_kernel<0><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, mode, out, ldw);
+        thermo_kernel<0><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, mode, out, ldw, 0);
     }
     return check_launch("slg_thermo_pack");
 }

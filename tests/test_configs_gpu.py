@@ -160,15 +160,14 @@ def test_c5_device_chunk_of_the_benchmark_vs_oracle(c5):
 
 # ------------------------------------------------------------------ soft
 def _soft_case(key, B):
-    """Model, raw input and the model-input transform of a config, for soft checks."""
-    import silogic_b200 as S
+    """Model and (host) model input of a config, for soft checks."""
     cfg = bench.CONFIGS[key]
     m, enc = bench.build_model(cfg)
     x = bench.make_input(cfg, B, seed=7)
     if cfg["inp"] == "bern":
         x = x.float()
     elif cfg["inp"] == "image":
-        x = S.binarize_spatial(x, cfg["thresholds"]).float()
+        x = torch.from_numpy(OH.thermometer_bits(x.numpy(), cfg["thresholds"])).float()
     return cfg, m, enc, x
 
 

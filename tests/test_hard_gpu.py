@@ -364,3 +364,54 @@ def test_device_index_check_names_the_first_bad_entry():
     x = torch.zeros(50, 2, dtype=torch.int64, device=dev)            # only 50 input rows
     with pytest.raises(IndexError, match="reads input row"):
         layer(x)
+
+
+@pytest.mark.parametrize("thr", [
+    [(i + 1) / 32 for i in range(31)],                       # C5's grid
+    [1 / 6, 2 / 6, 3 / 6, 4 / 6, 5 / 6],                      # C3's grid
+    [0.1 + 0.03 * i + (0.007 if i % 3 == 0 else -0.006) for i in range(20)],   # near uniform
+    [0.01, 0.02, 0.5, 0.51, 0.9],                             # far from uniform: searched
+    [0.3],                                                    # one threshold
+], ids=["grid31", "grid5", "perturbed20", "nonuniform5", "single"])
+def test_thermometer_pack_exact_at_threshold_boundaries(thr):
+    """binarize_spatial bits (x >= f32(t)) for values exactly at each threshold, one ulp
+    either side, +-inf and NaN, against the oracle: the sorted-threshold count (grid
+    guess corrected by two comparisons, or a binary search) must be exact."""
+    from silogic_b200 import _hard
+    t32 = np.asarray(thr, np.float32)
+    specials = np.concatenate([t32, np.nextafter(t32, -np.inf), np.nextafter(t32, np.inf),
+                               np.float32([np.inf, -np.inf, np.nan, 0.0, -0.0, 1.0, 2.0, -1.0])])
+    g = np.random.default_rng(len(thr))
+    B = 700
+    img = g.random((B, 3, 8, 8), dtype=np.float32)
+    flat = img.reshape(-1)
+    pick = g.choice(flat.size, size=flat.size // 3, replace=False)
+    flat[pick] = g.choice(specials, size=pick.size)
+    ref = OH.pack_bits(OH.thermometer_bits(img, thr).reshape(B, -1))
+    got = _hard.thermo_pack(torch.from_numpy(img).to(dev), list(thr))
+    got = got.reshape(got.shape[0] * got.shape[1] * got.shape[2], -1)[:, :ref.shape[1]]
+    np.testing.assert_array_equal(got.cpu().numpy().view(np.uint64), ref)
+
+
+@pytest.mark.parametrize("B", [100, 4096])
+def test_conv_gate_dispatch_kernel_equals_generic_tree_kernel(B):
+    """The arity-2 gate-dispatch conv kernel and the generic LUT-tree kernel give the
+    same bits (depths 1-3, pool 1 and 2, wire residual, image sizes down to 2x2)."""
+    from silogic_b200 import _hard, _lib
+    L = _lib.lib()
+    g = torch.Generator().manual_seed(B)
+    for depth, pool, C, H, n, wr in [(1, 2, 5, 9, 7, 0), (2, 2, 15, 32, 40, 0), (3, 1, 4, 6, 9, 0),
+                                     (2, 2, 16, 4, 24, 8), (2, 2, 8, 2, 300, 0)]:
+        ldw = _hard.ldw_for(B)
+        x = torch.randint(-2**62, 2**62, (C, H, H, ldw), generator=g).to(dev)
+        leaves = 2 ** depth
+        leaf = torch.randint(0, C * 9, (n, leaves), generator=g, dtype=torch.int32).to(dev)
+        tt = torch.randint(0, 16, (n, leaves - 1), generator=g).to(dev)
+        outs = []
+        for mode in (1, 0):
+            assert L.slg_tuning_set(0, mode) == 0
+            try:
+                outs.append(_hard.conv(x, leaf, tt, 2, depth, 3, 1, wr, pool))
+            finally:
+                L.slg_tuning_set(0, 1)
+        assert torch.equal(outs[0], outs[1]), (depth, pool, C, H, n, wr)
