@@ -181,6 +181,15 @@ int slg_packed_linear(const uint64_t* x, int64_t width, int64_t ldw, int64_t B, 
 #define SLG_NODE_MULTILINEAR 2 /* multilinear interpolation of sigmoid(logits)         */
 #define SLG_NODE_HYBRID 3      /* discrete forward, multilinear surrogate gradient     */
 #define SLG_NODE_LINEAR 4      /* sigmoid(theta_0 + sum_j theta_j a_j)                 */
+/* Node kinds whose parameters arrive already transformed, as the reference's fused-kernel
+ * functions pass them (silogic/kernels/dense.py:123, warp.py:104, multilinear.py:162,
+ * conv.py:399, conv_topk.py:175, conv_hybrid.py:196); arity 2 for the first two.  Their
+ * parameter gradients are with respect to those values (no softmax / sigmoid Jacobian). */
+#define SLG_NODE_COEF 5         /* c0 + c1 a + c2 b + c3 a b, params = 4 coefficients     */
+#define SLG_NODE_COEF_SIGMOID 6 /* sigmoid((c0 + c1 a + c2 b + c3 a b) * inv_tau)          */
+#define SLG_NODE_HYBRID_S 7     /* hybrid with LUT values s = sigmoid(logits) given        */
+/* conn_ste: 0 softmax(conn), 1 one-hot argmax (STE), 2 conn holds the weights themselves
+ * (gradients then with respect to the weights). */
 
 /* Soft forward of one FC logic layer on feature-major x [in_dim, ldb]:
  *   a_j[o,b] = sum_k w[o,j,k] x[cand[o,j,k], b],  w = softmax_k(conn[o,j,:])
@@ -278,6 +287,22 @@ int slg_conv_soft_bwd(const float* x, int64_t cin, int64_t H, int64_t W, int64_t
                       void* workspace, int64_t workspace_bytes, void* stream);
 
 /* -------------------------------------------------- soft-path boundaries */
+
+/* Deterministic form of slg_conv_soft_bwd for stride-1, pool-1 blocks without wire
+ * residual: the backward stores every leaf-candidate gradient once in `gleaf`
+ * (n_out*L*K*Ho*Wo*ldb floats, L = arity^depth) and a second kernel sums, for each
+ * input element, the entries of its channel in the caller's inverse map -- inv_off
+ * [cin+1] offsets into inv_ent [*, 4] int32 rows (n, l*K + k, dy - pad, dx - pad), in
+ * the order the caller fixes -- so gx (written, not accumulated) is bit-identical from
+ * run to run.  Replaces TreeConvAFFn.backward + build_inverse_map + _gather_gx
+ * (silogic/kernels/conv.py:247-351). */
+int slg_conv_soft_bwd_det(const float* x, int64_t cin, int64_t H, int64_t W, int64_t ldb,
+                          const int32_t* cand, const float* conn, int32_t K, int32_t conn_ste,
+                          int32_t node, int32_t arity, int32_t depth, const float* params,
+                          int32_t gate_hard, float inv_tau, int32_t kernel, int32_t pad,
+                          int64_t n_out, const float* gy, float* gx, float* gconn, float* gparams,
+                          const int32_t* inv_off, const int32_t* inv_ent, void* workspace,
+                          int64_t workspace_bytes, float* gleaf, int64_t gleaf_bytes, void* stream);
 
 /* [B, F] sample-major -> [F, ldb] feature-major (columns >= B zeroed), and back. */
 int slg_to_feature_major(const float* x, int64_t B, int64_t F, float* out, int64_t ldb,

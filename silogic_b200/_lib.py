@@ -39,6 +39,9 @@ _SIGS = {
                         _i64, _p, _p],
     "slg_fc_soft_bwd": [_p, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _p, _i32, _f32, _i64,
                         _i64, _p, _p, _p, _p, _p, _i64, _p],
+    "slg_conv_soft_bwd_det": [_p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _i32, _p,
+                              _i32, _f32, _i32, _i32, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p,
+                              _i64, _p],
     "slg_to_feature_major": [_p, _i64, _i64, _p, _i64, _p],
     "slg_from_feature_major": [_p, _i64, _i64, _i64, _p, _p],
     "slg_groupsum_soft_fwd": [_p, _i64, _i64, _i64, _i32, _f32, _i32, _p, _p],

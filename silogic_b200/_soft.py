@@ -273,11 +273,65 @@ class ConvSoft(torch.autograd.Function):
         xt, params, connc, arg = ctx.saved_tensors
         m = ctx.meta
         C, H, W = ctx.shape
+        if m.get("deterministic") and ctx.needs_input_grad[0]:
+            gx, gparams, gconn = conv_soft_bwd_deterministic(xt, (C, H, W), m, params, connc, gy)
+            return gx, gparams, gconn, None, None
         gx, gparams, gconn = op("conv_soft_bwd")(xt, C, H, W, m["cand"], connc, params,
                                                *ConvSoft._args(m), gy, arg,
                                                bool(ctx.needs_input_grad[0]))
         return (gx if ctx.needs_input_grad[0] else None, gparams,
                 gconn if connc is not None else None, None, None)
+
+
+def conv_inverse_map(cand, C, kernel, pad, K):
+    """For each input channel, the (output channel n, leaf candidate e = l*K + k, tap
+    dy - pad, tap dx - pad) rows that read it, ordered by (n, e): CSR offsets [C+1] and
+    [nnz, 4] int32 rows on cand's device (the inverse map of ``build_inverse_map``,
+    ``silogic/kernels/conv.py:247-265``, extended to Top-K candidates)."""
+    N = cand.shape[0]
+    flat = cand.reshape(N, -1).long()
+    LK = flat.shape[1]
+    kk = kernel * kernel
+    c = flat // kk
+    dy = (flat % kk) // kernel - pad
+    dx = flat % kernel - pad
+    n_idx = torch.arange(N, device=cand.device).unsqueeze(1).expand(N, LK)
+    e_idx = torch.arange(LK, device=cand.device).unsqueeze(0).expand(N, LK)
+    key = (c * N + n_idx) * LK + e_idx
+    order = torch.argsort(key.reshape(-1))
+    rows = torch.stack([n_idx.reshape(-1), e_idx.reshape(-1), dy.reshape(-1), dx.reshape(-1)], 1)
+    ent = rows[order].to(torch.int32).contiguous()
+    off = torch.zeros(C + 1, dtype=torch.int64, device=cand.device)
+    off[1:] = torch.cumsum(torch.bincount(c.reshape(-1), minlength=C), 0)
+    return off.to(torch.int32), ent
+
+
+def conv_soft_bwd_deterministic(xt, shape, m, params, connc, gy):
+    """Backward of one pool-1 conv block with a bit-reproducible input gradient
+    (``slg_conv_soft_bwd_det``: leaf gradients stored once, then gathered per input
+    element in inverse-map order)."""
+    from ._lib import call, lib, ptr, stream_ptr
+    C, H, W = shape
+    if m["pool"] != 1 or m["wire_r"]:
+        raise NotImplementedError("the deterministic conv backward covers pool-1 blocks without wire residual")
+    ldb = xt.shape[-1]
+    gy = gy.contiguous()
+    off, ent = conv_inverse_map(m["cand"], C, m["kernel"], m["pad"], m["K"])
+    gx = torch.empty_like(xt)
+    gparams = torch.empty_like(params)
+    gconn = torch.empty_like(connc) if connc is not None else None
+    nb = lib().slg_conv_soft_workspace_bytes(H, W, ldb, m["K"], m["node"], m["arity"], m["depth"],
+                                             m["kernel"], m["pad"], 1, m["n_out"])
+    ws = torch.empty(max(nb, 4) // 4 + 1, dtype=torch.float32, device=xt.device)
+    Ho, Wo = H + 2 * m["pad"] - m["kernel"] + 1, W + 2 * m["pad"] - m["kernel"] + 1
+    LK = m["cand"][0].numel()
+    gleaf = torch.empty(m["n_out"] * LK * Ho * Wo * ldb, dtype=torch.float32, device=xt.device)
+    call("slg_conv_soft_bwd_det", ptr(xt), C, H, W, ldb, ptr(m["cand"]), ptr(connc), m["K"],
+         m["ste"], m["node"], m["arity"], m["depth"], ptr(params), m["gate_hard"],
+         float(m["inv_tau"]), m["kernel"], m["pad"], m["n_out"], ptr(gy), ptr(gx), ptr(gconn),
+         ptr(gparams), ptr(off), ptr(ent), ptr(ws), ws.numel() * 4, ptr(gleaf),
+         gleaf.numel() * 4, stream_ptr(xt.device))
+    return gx, gparams, gconn
 
 
 def conv_block_fm(conv, xt, shape, wire_r=0, pool=1):

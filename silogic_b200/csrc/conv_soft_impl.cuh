@@ -40,8 +40,10 @@ struct TreeShape {
 
 template <int NODE, int AR>
 struct NodeStage {  // staged (transformed) parameter floats per node
-    static constexpr int NPS = NODE == N_GATE16 ? 4 : (NODE == N_LINEAR ? AR + 1 : (1 << AR) + 1);
-    static constexpr int RAW = NODE == N_GATE16 ? 16 : (NODE == N_LINEAR ? AR + 1 : (1 << AR));
+    static constexpr int NPS = (NODE == N_GATE16 || NODE == N_COEF) ? 4 : NODE == N_COEF_SIG ? 5
+                             : (NODE == N_LINEAR ? AR + 1 : (1 << AR) + 1);
+    static constexpr int RAW = NODE == N_GATE16 ? 16 : (NODE == N_COEF || NODE == N_COEF_SIG) ? 4
+                             : (NODE == N_LINEAR ? AR + 1 : (1 << AR));
 };
 
 template <int NODE, int AR, int D>
@@ -64,6 +66,10 @@ struct ConvArgs {
     // row-major order): written by the forward when non-null, read by the backward
     // instead of re-evaluating the window's trees
     uint8_t* pool_arg;
+    // deterministic backward (pool 1, no wire residual): when non-null the backward
+    // stores each leaf-candidate gradient gl * w at gleaf[((n*L*K + e)*Hp*Wp + p)*ldb + b]
+    // instead of adding it into gx with atomics; conv_leafgrad_gather sums them
+    float* gleaf;
 };
 
 // stage the channel's taps, weights and node parameters (whole block)
@@ -83,7 +89,9 @@ __device__ __forceinline__ void conv_stage(ConvSmem<NODE, AR, D>& S, const ConvA
     }
     // connection weights: warp w handles leaves w, w+8, ...
     for (int l = warp; l < L; l += CS_WARPS) {
-        if (A.conn) {
+        if (A.conn && A.conn_ste == 2) {        // weights given directly
+            for (int k = lane; k < K; k += 32) S.w[l * K + k] = A.conn[(n * L + l) * K + k];
+        } else if (A.conn) {
             if (lane == 0) {
                 const float* lg = A.conn + (n * L + l) * K;
                 float mx = lg[0];
@@ -372,7 +380,9 @@ conv_soft_bwd_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict
                         if (posq[e] >= 0) {
                             const int64_t idx = (int64_t)posq[e] * A.ldb + b;
                             acc_w[l * KT + k] += gl * (KEEP ? taps[l * KT + k] : __ldg(&A.x[idx]));
-                            if (gx && S.w[e] != 0.0f) atomicAdd(&gx[idx], gl * S.w[e]);
+                            if (A.gleaf)
+                                A.gleaf[((n * (L * K) + e) * (int64_t)npos + p) * A.ldb + b] = gl * S.w[e];
+                            else if (gx && S.w[e] != 0.0f) atomicAdd(&gx[idx], gl * S.w[e]);
                         }
                     }
                 }
@@ -420,7 +430,9 @@ __global__ void conv_soft_finish_kernel(const float* __restrict__ ws, int64_t ro
         const float* row = ws + (r * A.n_out + n) * npart;
         for (int e = 0; e < npart; ++e) tot[e] += row[e];
     }
-    if (gconn) {
+    if (gconn && A.conn_ste == 2) {             // weights given directly: dL/dw
+        for (int e = 0; e < L * K; ++e) gconn[n * L * K + e] = dead ? 0.f : tot[e];
+    } else if (gconn) {
         for (int l = 0; l < L; ++l) {
             const float* lg = A.conn + (n * L + l) * K;
             float mx = lg[0];
@@ -509,5 +521,8 @@ SLG_CONV_DISPATCH_DECL(walsh)
 SLG_CONV_DISPATCH_DECL(multi)
 SLG_CONV_DISPATCH_DECL(hybrid)
 SLG_CONV_DISPATCH_DECL(linear)
+SLG_CONV_DISPATCH_DECL(coef)
+SLG_CONV_DISPATCH_DECL(coef_sig)
+SLG_CONV_DISPATCH_DECL(hybrid_s)
 
 }  // namespace slg

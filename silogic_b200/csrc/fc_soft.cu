@@ -11,6 +11,8 @@ static bool fc_dispatch(int node, int arity, bool bwd, const FcArgs& A, float* y
         case N_MULTI: return fc_dispatch_multi(arity, bwd, A, y, gy, gx, ws, gconn, gparams, st);
         case N_HYBRID: return fc_dispatch_hybrid(arity, bwd, A, y, gy, gx, ws, gconn, gparams, st);
         case N_LINEAR: return fc_dispatch_linear(arity, bwd, A, y, gy, gx, ws, gconn, gparams, st);
+        case N_COEF: case N_COEF_SIG: case N_HYBRID_S:
+            return fc_dispatch_direct(node, arity, bwd, A, y, gy, gx, ws, gconn, gparams, st);
         default: return false;
     }
 }
@@ -22,7 +24,8 @@ static int check_fc(const FcArgs& A, int node, int arity, const char* name) {
     if (A.ldb % 4) return set_error(SLG_ERR_ALIGN, "%s: ldb must be a multiple of 4", name);
     if (!aligned16(A.x)) return set_error(SLG_ERR_ALIGN, "%s: x not 16-byte aligned", name);
     if (!A.cand || !A.params) return set_error(SLG_ERR_ARG, "%s: null pointer", name);
-    if (node == N_GATE16 && arity != 2) return set_error(SLG_ERR_ARG, "%s: gate16 is arity 2", name);
+    if (is_coef_node(node) && arity != 2) return set_error(SLG_ERR_ARG, "%s: node %d is arity 2", name, node);
+    if (A.conn_ste < 0 || A.conn_ste > 2) return set_error(SLG_ERR_ARG, "%s: conn_ste %d not in 0..2", name, A.conn_ste);
     if (A.wire_r > 0 && (A.wire_r > A.in_dim || A.wire_r > A.out_dim))
         return set_error(SLG_ERR_ARG, "%s: wire_r exceeds a width", name);
     if (cdiv(A.ldb / 4, 32 * FS_ITER) > 65535) return set_error(SLG_ERR_ARG, "%s: batch too large", name);
@@ -51,7 +54,7 @@ extern "C" int slg_fc_soft_fwd(const float* x, int64_t in_dim, int64_t ldb, cons
 extern "C" int64_t slg_fc_soft_workspace_bytes(int64_t ldb, int32_t K, int32_t node, int32_t arity,
                                                int64_t out_dim) {
     const int64_t nchunk = cdiv(ldb / 4, 32 * FS_ITER);
-    const int npg = node == N_GATE16 ? 4 : (node == N_LINEAR ? arity + 1 : (1 << arity));
+    const int npg = is_coef_node(node) ? 4 : (node == N_LINEAR ? arity + 1 : (1 << arity));
     return nchunk * out_dim * (int64_t)(arity * K + npg) * 4;
 }
 

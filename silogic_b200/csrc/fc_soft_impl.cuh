@@ -193,7 +193,7 @@ fc_soft_bwd_kernel(const float4* __restrict__ x, int64_t nv, const int32_t* __re
 // One thread per node.
 template <int NODE, int AR>
 __global__ void fc_soft_finish_kernel(const float* __restrict__ ws, int64_t nchunk, int64_t out_dim,
-                                      int npart, int K, const float* __restrict__ conn,
+                                      int npart, int K, const float* __restrict__ conn, int conn_ste,
                                       const float* __restrict__ params, int np_stride,
                                       int64_t wire_r, float* __restrict__ gconn,
                                       float* __restrict__ gparams) {
@@ -209,7 +209,9 @@ __global__ void fc_soft_finish_kernel(const float* __restrict__ ws, int64_t nchu
     }
     const bool dead = o < wire_r;
     // connection logits: softmax Jacobian (the soft weights also carry the STE gradient)
-    if (gconn) {
+    if (gconn && conn_ste == 2) {        // weights given directly: dL/dw as accumulated
+        for (int e = 0; e < AR * K; ++e) gconn[o * AR * K + e] = dead ? 0.0f : tot[e];
+    } else if (gconn) {
         for (int j = 0; j < AR; ++j) {
             const float* l = conn + (o * AR + j) * K;
             float mx = l[0];
@@ -257,7 +259,8 @@ struct FcArgs {
 };
 
 static inline int np_stride_of(int node, int ar) {
-    return node == N_GATE16 ? 16 : (node == N_LINEAR ? ar + 1 : (1 << ar));
+    return node == N_GATE16 ? 16 : (node == N_COEF || node == N_COEF_SIG) ? 4
+                                 : (node == N_LINEAR ? ar + 1 : (1 << ar));
 }
 
 template <int NODE, int AR, int KT>
@@ -281,8 +284,8 @@ inline void launch_bwd(const FcArgs& A, const float* gy, float* gx, float* ws, f
         np_stride_of(NODE, AR), A.gate_hard, A.inv_tau, A.out_dim, A.wire_r,
         reinterpret_cast<const float4*>(gy), reinterpret_cast<float4*>(gx), ws, npart);
     fc_soft_finish_kernel<NODE, AR><<<(unsigned)cdiv(A.out_dim, 128), 128, 0, st>>>(
-        ws, nchunk, A.out_dim, npart, A.K, A.conn, A.params, np_stride_of(NODE, AR), A.wire_r,
-        gconn, gparams);
+        ws, nchunk, A.out_dim, npart, A.K, A.conn, A.conn_ste, A.params, np_stride_of(NODE, AR),
+        A.wire_r, gconn, gparams);
 }
 
 // Per-node-kind dispatchers (each defined in its own translation unit so the
@@ -305,5 +308,6 @@ bool fc_dispatch_walsh(int arity, bool bwd, const FcArgs& A, float* y, const flo
 bool fc_dispatch_multi(int arity, bool bwd, const FcArgs& A, float* y, const float* gy, float* gx, float* ws, float* gconn, float* gparams, cudaStream_t st);
 bool fc_dispatch_hybrid(int arity, bool bwd, const FcArgs& A, float* y, const float* gy, float* gx, float* ws, float* gconn, float* gparams, cudaStream_t st);
 bool fc_dispatch_linear(int arity, bool bwd, const FcArgs& A, float* y, const float* gy, float* gx, float* ws, float* gconn, float* gparams, cudaStream_t st);
+bool fc_dispatch_direct(int node, int arity, bool bwd, const FcArgs& A, float* y, const float* gy, float* gx, float* ws, float* gconn, float* gparams, cudaStream_t st);
 
 }  // namespace slg

@@ -70,7 +70,7 @@ extern "C" int slg_fc_soft_bwd_noalloc(const float* x, int64_t in_dim, int64_t l
         return set_error(SLG_ERR_ARG, "slg_fc_soft_bwd_noalloc: bad sizes");
     if (K > FS_KMAX) return set_error(SLG_ERR_UNSUPPORTED, "slg_fc_soft_bwd_noalloc: K=%d > %d", K, FS_KMAX);
     if (ldb % 4) return set_error(SLG_ERR_ALIGN, "slg_fc_soft_bwd_noalloc: ldb must be a multiple of 4");
-    if (node < N_GATE16 || node > N_LINEAR || arity < 1 || arity > 6 || (node == N_GATE16 && arity != 2))
+    if (node < N_GATE16 || node > N_HYBRID_S || arity < 1 || arity > 6 || (is_coef_node(node) && arity != 2))
         return set_error(SLG_ERR_ARG, "slg_fc_soft_bwd_noalloc: node %d arity %d", node, arity);
     const int64_t need = slg_fc_soft_workspace_bytes(ldb, K, node, arity, out_dim);
     if (need > kNoallocScratchBytes)

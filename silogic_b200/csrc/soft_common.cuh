@@ -1,18 +1,30 @@
 // Soft (relaxed, fp32) node math shared by the FC and conv kernels.
 //
-// Node kinds (slg node enum): 0 gate16, 1 walsh, 2 multilinear, 3 hybrid, 4 linear.
+// Node kinds (slg node enum): 0 gate16, 1 walsh, 2 multilinear, 3 hybrid, 4 linear, and
+// three kinds whose parameters arrive already transformed (the reference's fused-kernel
+// functions take them that way): 5 coef (BasisProj coefficients), 6 coef-sigmoid
+// (Walsh in BasisProj form), 7 hybrid with LUT values s = sigmoid(logits) given.
 // "np" is the per-node transformed parameter vector staged in shared memory:
 //   gate16      : c[4]   = gate_probs(logits) @ basis   (forward value; STE one-hot when hard)
 //   walsh       : theta[P], then inv_tau at np[P]
 //   multilinear : s[P]   = sigmoid(logits)
 //   hybrid      : s[P]
 //   linear      : theta[AR+1]
+//   coef        : c[4]   (as given)
+//   coef-sigmoid: c[4], then inv_tau at np[4]
+//   hybrid-s    : s[P]   (as given)
 #pragma once
 #include "common.cuh"
 
 namespace slg {
 
-enum NodeKind { N_GATE16 = 0, N_WALSH = 1, N_MULTI = 2, N_HYBRID = 3, N_LINEAR = 4 };
+enum NodeKind { N_GATE16 = 0, N_WALSH = 1, N_MULTI = 2, N_HYBRID = 3, N_LINEAR = 4,
+                N_COEF = 5, N_COEF_SIG = 6, N_HYBRID_S = 7 };
+
+// nodes whose operands are exactly two inputs in (a, b) BasisProj form
+__host__ __device__ constexpr bool is_coef_node(int node) {
+    return node == N_GATE16 || node == N_COEF || node == N_COEF_SIG;
+}
 
 // BasisProj coefficients of the 16 gates (1, a, b, a*b), DiffLogic order.
 __constant__ float c_basis[16][4] = {
@@ -26,15 +38,17 @@ __device__ __forceinline__ float sigmoidf_(float z) { return 1.0f / (1.0f + expf
 template <int NODE, int AR>
 struct NodeSize {
     static constexpr int P = 1 << AR;
-    static constexpr int NPG = NODE == N_GATE16 ? 4 : (NODE == N_LINEAR ? AR + 1 : P);
+    static constexpr int NPG = is_coef_node(NODE) ? 4 : (NODE == N_LINEAR ? AR + 1 : P);
 };
 
 // ------------------------------------------------------------------ forward
 template <int NODE, int AR>
 __device__ __forceinline__ float node_fwd(const float* __restrict__ np, const float (&a)[AR]) {
     constexpr int P = 1 << AR;
-    if constexpr (NODE == N_GATE16) {
+    if constexpr (NODE == N_GATE16 || NODE == N_COEF) {
         return np[0] + np[1] * a[0] + np[2] * a[1] + np[3] * (a[0] * a[1]);
+    } else if constexpr (NODE == N_COEF_SIG) {
+        return sigmoidf_((np[0] + np[1] * a[0] + np[2] * a[1] + np[3] * (a[0] * a[1])) * np[4]);
     } else if constexpr (NODE == N_WALSH) {
         float m[P];
         m[0] = 1.0f;
@@ -57,7 +71,7 @@ __device__ __forceinline__ float node_fwd(const float* __restrict__ np, const fl
 #pragma unroll
             for (int q = 0; q < (P >> (j + 1)); ++q) t[q] = t[2 * q] + a[j] * (t[2 * q + 1] - t[2 * q]);
         return t[0];
-    } else if constexpr (NODE == N_HYBRID) {
+    } else if constexpr (NODE == N_HYBRID || NODE == N_HYBRID_S) {
         int idx = 0;
 #pragma unroll
         for (int j = 0; j < AR; ++j) idx |= (a[j] >= 0.5f ? 1 : 0) << j;
@@ -77,13 +91,23 @@ template <int NODE, int AR>
 __device__ __forceinline__ void node_bwd(const float* __restrict__ np, const float (&a)[AR], float gy,
                                          float (&ga)[AR], float (&acc)[NodeSize<NODE, AR>::NPG]) {
     constexpr int P = 1 << AR;
-    if constexpr (NODE == N_GATE16) {
+    if constexpr (NODE == N_GATE16 || NODE == N_COEF) {
         ga[0] = gy * (np[1] + np[3] * a[1]);
         ga[1] = gy * (np[2] + np[3] * a[0]);
         acc[0] += gy;
         acc[1] += gy * a[0];
         acc[2] += gy * a[1];
         acc[3] += gy * (a[0] * a[1]);
+    } else if constexpr (NODE == N_COEF_SIG) {
+        const float it = np[4];
+        const float y = sigmoidf_((np[0] + np[1] * a[0] + np[2] * a[1] + np[3] * (a[0] * a[1])) * it);
+        const float dz = gy * y * (1.0f - y) * it;
+        ga[0] = dz * (np[1] + np[3] * a[1]);
+        ga[1] = dz * (np[2] + np[3] * a[0]);
+        acc[0] += dz;
+        acc[1] += dz * a[0];
+        acc[2] += dz * a[1];
+        acc[3] += dz * (a[0] * a[1]);
     } else if constexpr (NODE == N_WALSH) {
         float u[AR];
 #pragma unroll
@@ -111,7 +135,7 @@ __device__ __forceinline__ void node_bwd(const float* __restrict__ np, const flo
                 if (q & (1 << j)) d += np[q] * m[q ^ (1 << j)];
             ga[j] = 2.0f * dz * d;
         }
-    } else if constexpr (NODE == N_MULTI || NODE == N_HYBRID) {
+    } else if constexpr (NODE == N_MULTI || NODE == N_HYBRID || NODE == N_HYBRID_S) {
         // reverse mode through the lerp tree; leaf adjoints are the LUT-entry weights
         float lv[2 * P];      // lv[P + q]: level-0 leaves live in np; levels 1.. in lv[P >> l ...]
         // level l (1..AR) has P >> l nodes stored at lv[(P >> l) + q]
@@ -188,6 +212,13 @@ __device__ __forceinline__ void stage_node_params(const float* __restrict__ raw,
                 np[c] = v;
             }
         }
+    } else if constexpr (NODE == N_COEF) {
+        if (lane < 4) np[lane] = raw[lane];
+    } else if constexpr (NODE == N_COEF_SIG) {
+        if (lane < 4) np[lane] = raw[lane];
+        if (lane == 0) np[4] = inv_tau;
+    } else if constexpr (NODE == N_HYBRID_S) {
+        for (int q = lane; q < P; q += 32) np[q] = raw[q];
     } else if constexpr (NODE == N_WALSH) {
         for (int q = lane; q < P; q += 32) np[q] = raw[q];
         if (lane == 0) np[P] = inv_tau;
@@ -199,10 +230,16 @@ __device__ __forceinline__ void stage_node_params(const float* __restrict__ raw,
     __syncwarp();
 }
 
-// Connection weights of one node: softmax over K per slot (one-hot when ste).
+// Connection weights of one node: softmax over K per slot (one-hot when ste == 1; the
+// values as given when ste == 2, i.e. already-normalised weights).
 // w[j*K + k]; executed by lanes j < AR.
 __device__ __forceinline__ void stage_conn(const float* __restrict__ logits, float* w, int AR, int K,
                                            int ste, int lane) {
+    if (ste == 2) {
+        for (int e = lane; e < AR * K; e += 32) w[e] = logits[e];
+        __syncwarp();
+        return;
+    }
     if (lane < AR) {
         const float* l = logits + lane * K;
         float mx = l[0];

@@ -115,3 +115,14 @@ def test_chain_layout_bank_grouping_preserves_the_circuit(kw):
                 slots = np.unique((r[g:g + 16] >> sh) & 0x3fff)
                 assert np.bincount(slots % 16, minlength=16).max() <= 1
         off += w
+
+
+def test_build_inverse_map_lists_every_reader_in_order():
+    import silogic_b200.kernels as K
+    cm = torch.tensor([[0, 2], [1, 0]], dtype=torch.int32)
+    ch = torch.tensor([[0, 1], [2, 1]], dtype=torch.int32)
+    cw = torch.tensor([[1, 2], [0, 0]], dtype=torch.int32)
+    off, en, el, edy, edx = K.build_inverse_map(cm, ch, cw, 3)
+    assert off.tolist() == [0, 2, 3, 4]
+    assert list(zip(en.tolist(), el.tolist())) == [(0, 0), (1, 1), (1, 0), (0, 1)]
+    assert edy.tolist() == [0, 1, 2, 1] and edx.tolist() == [1, 0, 0, 2]
