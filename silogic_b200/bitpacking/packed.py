@@ -78,6 +78,11 @@ class BitpackedGPULayer(PackedFCLayer):
 
     @classmethod
     def from_fc_layer(cls, fc_layer, device="cuda"):
+        """From a converted FC layer: this package's (wiring + truth tables) or one with the
+        reference ``BitpackedFCLayer`` fields ``gate_types`` / ``a_idx`` / ``b_idx``
+        (``triton_layer.py:176-179``)."""
+        if hasattr(fc_layer, "gate_types"):
+            return cls(fc_layer.gate_types, fc_layer.a_idx, fc_layer.b_idx, device)
         obj = cls.__new__(cls)
         PackedFCLayer.__init__(obj, fc_layer.idx.to(device), fc_layer.tt.to(device))
         obj.device = device

@@ -20,6 +20,12 @@
 namespace slg {
 
 constexpr int G2_THREADS = 256;
+#ifndef SLG_G2_PRELOAD
+#define SLG_G2_PRELOAD 1        // depth 2: load all four leaves before the first node
+#endif
+#ifndef SLG_G2_MINB
+#define SLG_G2_MINB 2           // minimum resident CTAs per SM requested from the compiler
+#endif
 
 // f(a, b) for the 4-bit table T, address a | b << 1 (slot 0 = the lower child), as a
 // single three-input logic op after constant folding.
@@ -124,7 +130,7 @@ __device__ __forceinline__ void eval_d2(const G2Ctx<4, POOL>& c, const uint32_t*
 }
 
 template <int DEPTH, int POOL>
-__global__ void __launch_bounds__(G2_THREADS, 2)
+__global__ void __launch_bounds__(G2_THREADS, SLG_G2_MINB)
 conv_gate2_kernel(const uint4* __restrict__ x, int H, int W, int nvec, const int32_t* __restrict__ leaf,
                   const uint64_t* __restrict__ tt, int kernel, int pad, int64_t n_out, int64_t wire_r,
                   int Hp, int Wp, uint4* __restrict__ out, int vt_shift, int slot_shift, int ppt,
@@ -189,7 +195,7 @@ conv_gate2_kernel(const uint4* __restrict__ x, int H, int W, int nvec, const int
         const bool inside = y0 - pad >= 0 && y0 + POOL - 1 + kernel - 1 - pad < H &&
                             x0 - pad >= 0 && x0 + POOL - 1 + kernel - 1 - pad < W;
         uint32_t r[NWORD];
-        if constexpr (DEPTH == 2) {
+        if constexpr (DEPTH == 2 && SLG_G2_PRELOAD) {
             if (inside) eval_d2<POOL, false>(c, codes, y0, x0, pn, r);
             else eval_d2<POOL, true>(c, codes, y0, x0, pn, r);
         } else {

@@ -1,8 +1,8 @@
 """The reference's fused-kernel function API (``silogic.kernels``) on the CUDA kernels,
 against plain torch fp32 restatements of the reference's formulas
 (``silogic/kernels/{dense,warp,multilinear,conv,conv_topk,conv_hybrid}.py``): forward
-values within 1e-5 relative, gradients with respect to every tensor argument within
-1e-5 (|ref| + max|ref|)."""
+values and the gradients with respect to every tensor argument within
+1e-5 (|ref| + max|ref|) + 1e-7 (fp32; the summation order differs)."""
 import numpy as np
 import pytest
 import torch
@@ -20,8 +20,7 @@ def _leaf(t):
 
 
 def _check(got, ref, inputs_got, inputs_ref, gout):
-    np.testing.assert_allclose(got.detach().cpu().numpy(), ref.detach().cpu().numpy(),
-                               rtol=1e-5, atol=1e-6)
+    assert_grad_close(got, ref.detach().numpy(), "forward")
     (got * gout.to(dev)).sum().backward()
     (ref * gout).sum().backward()
     for i, (a, b) in enumerate(zip(inputs_got, inputs_ref)):
@@ -71,7 +70,9 @@ def _hybrid(ops, s):
     au = ops.unsqueeze(-2)                                          # [..., 1, n]
     soft = ((c * au + (1 - c) * (1 - au)).prod(-1) * s).sum(-1)
     idx = ((ops >= 0.5).long() << torch.arange(n)).sum(-1, keepdim=True)
-    disc = torch.gather(s.expand(*ops.shape[:-1], s.shape[-1]), -1, idx).squeeze(-1)
+    # the discrete value carries no gradient (HybridNode evaluates it under no_grad, and
+    # the fused kernel's s-gradient is the soft surrogate's alone)
+    disc = torch.gather(s.detach().expand(*ops.shape[:-1], s.shape[-1]), -1, idx).squeeze(-1)
     return disc + soft - soft.detach()
 
 
