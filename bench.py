@@ -282,7 +282,11 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
     launches = [0]
     nchunks = (B + chunk - 1) // chunk
     counts_all = torch.empty((B, plan.num_classes), dtype=torch.int32, device=dev)
-    gathered = torch.empty((ws * B, plan.num_classes), dtype=torch.int32, device=dev) if ws > 1 else None
+    # counts cross NVLink in the narrowest type that holds them (int16 for <= 32767 per class)
+    from silogic_b200.distributed import wire_dtype
+    last = plan.steps[-1]
+    wdt = wire_dtype(last["idx"].shape[0] // plan.num_classes if last["op"] == "fc" else 1 << 30)
+    gathered = torch.empty((ws * B, plan.num_classes), dtype=wdt, device=dev) if ws > 1 else None
     mode = 0 if cfg["inp"] == "image" else 1
 
     def pack_chunk(n):
@@ -343,7 +347,7 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
             counts_all[c * chunk:c * chunk + n].copy_(graphs[n].replay())
             launches[0] += 2 if uses_chain(n) else 2 + len(plan.steps)
         if ws > 1 and collective:   # only the class counts leave the GPU
-            torch.distributed.all_gather_into_tensor(gathered, counts_all)
+            torch.distributed.all_gather_into_tensor(gathered, counts_all.to(wdt))
         return counts_all
 
     def step_e2e():
@@ -811,7 +815,7 @@ def main():
             "dtype": "u64", "data": "synthetic (seeded inputs, N(0,1) parameters)",
             "config": {"workload": cfg["name"], "batch_per_gpu": res["B"],
                        "global_batch": res["total"],
-                       "parallelism": f"batch shard x{ws}, counts all-gathered",
+                       "parallelism": f"batch shard x{ws}, counts all-gathered (int16 on the wire)",
                        "l2": "flushed before each step (256 MB write, then read back so L2 is clean)",
                        "launch": "one CUDA graph per chunk shape (pack + every layer + GroupSum)",
                        "clocks": "sampled over >= 1 s of untimed replays of the same step, then the timed steps"},

@@ -88,13 +88,14 @@ def _acc(logits, y):
     return float((logits.argmax(1) == y).mean())
 
 
-def _run(model, bp, x_test, y_test, batch_sizes, device, n_warmup, n_runs):
+def _run(model, convert, x_test, y_test, batch_sizes, device, n_warmup, n_runs):
     if not str(device).startswith("cuda"):
         raise RuntimeError("silogic_b200 runs on CUDA only (no CPU implementation); pass device='cuda'")
     results: List[BenchResult] = []
     model.eval()
     dev = torch.device(device)
     model.to(dev)
+    bp = convert(model)
     for B in batch_sizes:
         idx = np.arange(B) % len(x_test)
         x_b = np.ascontiguousarray(x_test[idx])
@@ -121,7 +122,7 @@ def run_benchmark(model, x_test: np.ndarray, y_test: Optional[np.ndarray],
     """Benchmark a ``LogicNet``: soft, hard and bit-packed inference on ``x_test``
     ``[N, in_dim]`` uint8 (``benchmark.py:84-211``).  ``include_gpu`` is accepted for
     signature parity: every path here is a GPU path."""
-    return _run(model, convert_logic_net(model), x_test, y_test, batch_sizes, device,
+    return _run(model, convert_logic_net, x_test, y_test, batch_sizes, device,
                 n_warmup, n_runs)
 
 
@@ -132,7 +133,7 @@ def run_conv_benchmark(model, x_test: np.ndarray, y_test: Optional[np.ndarray],
                        n_runs: int = 20) -> List[BenchResult]:
     """Benchmark a ``LogicConvNet`` on ``x_test`` ``[N, C, H, W]`` uint8
     (``benchmark.py:249-367``)."""
-    return _run(model, convert_logic_conv_net(model), x_test, y_test, batch_sizes, device,
+    return _run(model, convert_logic_conv_net, x_test, y_test, batch_sizes, device,
                 n_warmup, n_runs)
 
 

@@ -260,40 +260,48 @@ thermo_kernel(const float* __restrict__ x, int64_t B, int64_t C, int64_t HW,
         // is [c_i > t] over i.  Instead of a 32x32 bit transpose of thermometer masks,
         // ballot the LB bits of c (bit-sliced counts, one word per bit), and each lane
         // compares the bit-sliced count with its own t, one logic op per bit.
+        // A count lies in [0, nt] and nt < 2^LOG (the host sizes LOG so), so LOG bits hold it.
         const bool sliced = LOG > 0 && grp == 1;
-        int lb = 0;
-        while ((1 << lb) <= nt) ++lb;                       // bits of a count in [0, nt]
-        uint32_t tmaskb[6];
+        constexpr int LB = LOG > 0 ? LOG : 1;
+        uint32_t tmaskb[LB];
 #pragma unroll
-        for (int k = 0; k < 6; ++k) tmaskb[k] = ((lt >> k) & 1) ? 0xffffffffu : 0u;
+        for (int k = 0; k < LB; ++k) tmaskb[k] = ((lt >> k) & 1) ? 0xffffffffu : 0u;
         for (int item = warp; item < ngroups * 2; item += 8) {
             const int g = item >> 1, wp = item & 1;       // feature group, word pair
             const int fa = g * grp;
             uint32_t wd[4];
-            if (sliced) {
+            if (sliced && uni) {
 #pragma unroll
                 for (int h = 0; h < 4; ++h) {
                     const float v = tile[wp * 128 + h * 32 + lane][fa];
-                    int pos;
-                    if (uni) {
-                        // nearest integer of q + 1/2 (exact float rounding, no conversion
-                        // unit): within one of the count, as the comment above requires
-                        const float q = fminf(fmaxf((v - u0) * inv + 0.5f, 0.f), 64.f);
-                        const int gi = min(__float_as_int(q + 12582912.0f) - 0x4B400000, nt);
-                        pos = gi + (int)(v >= s_pad[gi + 1]) - (int)(v < s_pad[gi]);
-                    } else {
-                        pos = 0;
+                    // nearest integer of q + 1/2 (exact float rounding, no conversion
+                    // unit): within one of the count, as the comment above requires
+                    const float q = fminf(fmaxf((v - u0) * inv + 0.5f, 0.f), 64.f);
+                    const int gi = min(__float_as_int(q + 12582912.0f) - 0x4B400000, nt);
+                    const int pos = gi + (int)(v >= s_pad[gi + 1]) - (int)(v < s_pad[gi]);
+                    const uint32_t ok = __ballot_sync(0xffffffffu, b0 + wp * 128 + h * 32 + lane < B);
+                    uint32_t gt = 0u;
 #pragma unroll
-                        for (int st = (LOG > 0 ? LOG : 1) - 1; st >= 0; --st) {
-                            const int np = pos + (1 << st);
-                            if (v >= s_srt[np - 1]) pos = np;
-                        }
+                    for (int k = 0; k < LB; ++k) {
+                        const uint32_t bk = __ballot_sync(0xffffffffu, (pos >> k) & 1);
+                        gt = (bk & gt & tmaskb[k]) | ((bk | gt) & ~tmaskb[k]);
+                    }
+                    wd[h] = gt & ok;
+                }
+            } else if (sliced) {
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    const float v = tile[wp * 128 + h * 32 + lane][fa];
+                    int pos = 0;
+#pragma unroll
+                    for (int st = (LOG > 0 ? LOG : 1) - 1; st >= 0; --st) {
+                        const int np = pos + (1 << st);
+                        if (v >= s_srt[np - 1]) pos = np;
                     }
                     const uint32_t ok = __ballot_sync(0xffffffffu, b0 + wp * 128 + h * 32 + lane < B);
                     uint32_t gt = 0u;
 #pragma unroll
-                    for (int k = 0; k < 6; ++k) {
-                        if (k >= lb) break;
+                    for (int k = 0; k < LB; ++k) {
                         const uint32_t bk = __ballot_sync(0xffffffffu, (pos >> k) & 1);
                         gt = (bk & gt & tmaskb[k]) | ((bk | gt) & ~tmaskb[k]);
                     }

@@ -22,17 +22,28 @@ def shard_range(total, world_size, rank, align=64):
     return min(total, u0 * align), min(total, u1 * align)
 
 
-def gather_counts(local_counts, total, group=None):
-    """All-gather per-rank ``[b_r, C]`` counts into ``[total, C]`` in rank order."""
+def wire_dtype(max_count):
+    """Narrowest integer type that carries counts up to ``max_count`` (a class count is at
+    most the group size, e.g. 1,000 for a 10,000-wide layer and 10 classes): int16
+    halves the bytes of the gather against int32."""
+    return torch.int16 if max_count <= 32767 else torch.int32
+
+
+def gather_counts(local_counts, total, group=None, max_count=None):
+    """All-gather per-rank ``[b_r, C]`` counts into ``[total, C]`` in rank order.  With
+    ``max_count`` the counts travel in :func:`wire_dtype` and come back in the input's
+    dtype."""
     ws = dist.get_world_size(group)
     C = local_counts.shape[1]
     sizes = [shard_range(total, ws, r)[1] - shard_range(total, ws, r)[0] for r in range(ws)]
     mx = max(sizes)
-    buf = torch.zeros((mx, C), dtype=local_counts.dtype, device=local_counts.device)
+    wd = wire_dtype(max_count) if max_count is not None else local_counts.dtype
+    buf = torch.zeros((mx, C), dtype=wd, device=local_counts.device)
     buf[:local_counts.shape[0]] = local_counts
-    parts = [torch.empty_like(buf) for _ in range(ws)]
-    dist.all_gather(parts, buf, group=group)
-    return torch.cat([p[:n] for p, n in zip(parts, sizes)], 0)
+    raw = buf.view(torch.uint8)                 # bytes on the wire (any backend moves uint8)
+    parts = [torch.empty_like(raw) for _ in range(ws)]
+    dist.all_gather(parts, raw, group=group)
+    return torch.cat([p.view(wd)[:n] for p, n in zip(parts, sizes)], 0).to(local_counts.dtype)
 
 
 def sharded_hard_counts(plan, x, group=None):
@@ -44,7 +55,10 @@ def sharded_hard_counts(plan, x, group=None):
     a, b = shard_range(x.shape[0], ws, rank)
     local = plan.counts(x[a:b]) if b > a else torch.zeros(
         (0, plan.num_classes), dtype=torch.int32, device=x.device)
-    return gather_counts(local, x.shape[0], group)
+    steps = getattr(plan, "steps", None)
+    width = steps[-1]["idx"].shape[0] if steps and steps[-1]["op"] == "fc" else None
+    max_count = width // plan.num_classes if width and plan.num_classes else None
+    return gather_counts(local, x.shape[0], group, max_count)
 
 
 def allreduce_gradients(params, group=None, average=True):

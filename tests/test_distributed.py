@@ -48,6 +48,11 @@ def _worker_gather(rank, ws, port, q):
         counts = torch.arange(a, b, dtype=torch.int32).view(-1, 1).repeat(1, 10)
         full = D.gather_counts(counts, total)
         ok = torch.equal(full[:, 0], torch.arange(total, dtype=torch.int32))
+        # counts up to 1000 travel as int16 and come back as int32, unchanged
+        small = (counts % 1000).contiguous()
+        narrow = D.gather_counts(small, total, max_count=1000)
+        ok = ok and narrow.dtype == torch.int32 and torch.equal(narrow[:, 0], torch.arange(total) % 1000)
+        ok = ok and D.wire_dtype(1000) == torch.int16 and D.wire_dtype(40000) == torch.int32
         # gradient all-reduce: each rank contributes rank+1
         p = torch.nn.Parameter(torch.zeros(3, 4))
         p.grad = torch.full((3, 4), float(rank + 1))
