@@ -389,8 +389,9 @@ def test_thermometer_pack_exact_at_threshold_boundaries(thr):
     flat[pick] = g.choice(specials, size=pick.size)
     ref = OH.pack_bits(OH.thermometer_bits(img, thr).reshape(B, -1))
     got = _hard.thermo_pack(torch.from_numpy(img).to(dev), list(thr))
-    got = got.reshape(got.shape[0] * got.shape[1] * got.shape[2], -1)[:, :ref.shape[1]]
-    np.testing.assert_array_equal(got.cpu().numpy().view(np.uint64), ref)
+    got = got.reshape(got.shape[0] * got.shape[1] * got.shape[2], -1)
+    np.testing.assert_array_equal(got[:, :ref.shape[1]].cpu().numpy().view(np.uint64), ref)
+    assert not got[:, ref.shape[1]:].any(), "padding words must be zero"
 
 
 @pytest.mark.parametrize("B", [100, 4096])
