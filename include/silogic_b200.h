@@ -90,9 +90,7 @@ int slg_check_index_range(const int32_t* idx, int64_t count, int64_t limit, void
  *          generic LUT-tree kernel (0); both give identical bits;
  *   key 1  pooled positions per thread in that kernel (8);
  *   key 2  sorted near-uniform thermometer thresholds use the grid guess with two
- *          corrective comparisons (1) or a binary search (0); both give identical bits;
- *   key 3  depth-2 gate-dispatch conv trees evaluate two pooled positions per node
- *          branch (1) or one (0); both give identical bits.
+ *          corrective comparisons (1) or a binary search (0); both give identical bits.
  * No counterpart in the reference (its Triton kernels take fixed block sizes). */
 int slg_tuning_set(int32_t key, int64_t value);
 

@@ -129,46 +129,8 @@ __device__ __forceinline__ void eval_d2(const G2Ctx<4, POOL>& c, const uint32_t*
     node_apply(codes[2], r, d);
 }
 
-// Leaf l of the window at (y0, x0) into words [OFF, OFF + 4 POOL^2) of a larger array.
-template <int OFF, int POOL, bool CHECK, int N>
-__device__ __forceinline__ void load_leaf_to(const G2Ctx<4, POOL>& c, int l, int y0, int x0, int pn,
-                                             uint32_t (&v)[N]) {
-#pragma unroll
-    for (int s = 0; s < POOL * POOL; ++s) {
-        uint4 t = make_uint4(0, 0, 0, 0);
-        const int oy = s / POOL, ox = s % POOL;
-        if (!CHECK || ((unsigned)(y0 + oy + c.ly[l]) < (unsigned)c.H &&
-                       (unsigned)(x0 + ox + c.lx[l]) < (unsigned)c.W))
-            t = __ldg(c.lp[l] + (pn + c.dpn[l] + c.soff[s]));
-        v[OFF + 4 * s + 0] = t.x; v[OFF + 4 * s + 1] = t.y; v[OFF + 4 * s + 2] = t.z; v[OFF + 4 * s + 3] = t.w;
-    }
-}
-
-// Depth 2 over two pooled positions per node branch (32 words): the uniform branch on
-// each node's code, which the compiler lowers to a chain of compares, is paid once per
-// 32 words.  Leaves are loaded a pair at a time to bound the live registers.
-template <int POOL, bool CHECK>
-__device__ __forceinline__ void eval_d2_pair(const G2Ctx<4, POOL>& c, const uint32_t* codes, int ya,
-                                             int xa, int pna, int yb, int xb, int pnb,
-                                             uint32_t (&r)[2 * POOL * POOL * 4]) {
-    constexpr int H = POOL * POOL * 4;
-    uint32_t b[2 * H];
-    load_leaf_to<0, POOL, CHECK>(c, 0, ya, xa, pna, r);
-    load_leaf_to<H, POOL, CHECK>(c, 0, yb, xb, pnb, r);
-    load_leaf_to<0, POOL, CHECK>(c, 1, ya, xa, pna, b);
-    load_leaf_to<H, POOL, CHECK>(c, 1, yb, xb, pnb, b);
-    node_apply(codes[0], r, b);
-    uint32_t d[2 * H];
-    load_leaf_to<0, POOL, CHECK>(c, 2, ya, xa, pna, d);
-    load_leaf_to<H, POOL, CHECK>(c, 2, yb, xb, pnb, d);
-    load_leaf_to<0, POOL, CHECK>(c, 3, ya, xa, pna, b);
-    load_leaf_to<H, POOL, CHECK>(c, 3, yb, xb, pnb, b);
-    node_apply(codes[1], d, b);
-    node_apply(codes[2], r, d);
-}
-
-template <int DEPTH, int POOL, bool PAIR>
-__global__ void __launch_bounds__(G2_THREADS, PAIR ? 1 : SLG_G2_MINB)
+template <int DEPTH, int POOL>
+__global__ void __launch_bounds__(G2_THREADS, SLG_G2_MINB)
 conv_gate2_kernel(const uint4* __restrict__ x, int H, int W, int nvec, const int32_t* __restrict__ leaf,
                   const uint64_t* __restrict__ tt, int kernel, int pad, int64_t n_out, int64_t wire_r,
                   int Hp, int Wp, uint4* __restrict__ out, int vt_shift, int slot_shift, int ppt,
@@ -231,35 +193,7 @@ conv_gate2_kernel(const uint4* __restrict__ x, int H, int W, int nvec, const int
         return y0 - pad >= 0 && y0 + POOL - 1 + kernel - 1 - pad < H &&
                x0 - pad >= 0 && x0 + POOL - 1 + kernel - 1 - pad < W;
     };
-    int pos = pos0;
-    if constexpr (DEPTH == 2 && PAIR) {
-        {
-            for (; pos + 1 < pend; pos += 2) {
-                const int ya = py * POOL, xa = px * POOL;
-                if (++px == Wp) { px = 0; ++py; }
-                const int yb = py * POOL, xb = px * POOL;
-                if (++px == Wp) { px = 0; ++py; }
-                const int pna = (ya * W + xa) * nvec, pnb = (yb * W + xb) * nvec;
-                uint32_t r[2 * NWORD];
-                if (interior(ya, xa) && interior(yb, xb))
-                    eval_d2_pair<POOL, false>(c, codes, ya, xa, pna, yb, xb, pnb, r);
-                else
-                    eval_d2_pair<POOL, true>(c, codes, ya, xa, pna, yb, xb, pnb, r);
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    uint4 acc = make_uint4(r[h * NWORD], r[h * NWORD + 1], r[h * NWORD + 2], r[h * NWORD + 3]);
-#pragma unroll
-                    for (int s = 1; s < POOL * POOL; ++s) {
-                        acc.x |= r[h * NWORD + 4 * s]; acc.y |= r[h * NWORD + 4 * s + 1];
-                        acc.z |= r[h * NWORD + 4 * s + 2]; acc.w |= r[h * NWORD + 4 * s + 3];
-                    }
-                    *dst = acc;
-                    dst += nvec;
-                }
-            }
-        }
-    }
-    for (; pos < pend; ++pos) {
+    for (int pos = pos0; pos < pend; ++pos) {
         const int y0 = py * POOL, x0 = px * POOL;
         const int pn = (y0 * W + x0) * nvec;
         const bool inside = interior(y0, x0);
@@ -307,16 +241,11 @@ bool launch_conv_gate2(const uint4* x, int64_t cin, int H, int W, int nvec, cons
     const int64_t tiles = cdiv(npos, slots * ppt);
     if (gy > 65535 || n_out * tiles > 0x7fffffffLL) return false;
     dim3 grid((unsigned)(n_out * tiles), (unsigned)gy);
-#define SLG_G2(D, P, Q) conv_gate2_kernel<D, P, Q><<<grid, G2_THREADS, 0, st>>>(x, H, W, nvec, leaf, tt, kernel, pad, n_out, wire_r, Hp, Wp, out, vs, ss, (int)ppt, (int)tiles)
-    const bool pair = tuning(T_CONV_PAIR) != 0;
+#define SLG_G2(D, P) conv_gate2_kernel<D, P><<<grid, G2_THREADS, 0, st>>>(x, H, W, nvec, leaf, tt, kernel, pad, n_out, wire_r, Hp, Wp, out, vs, ss, (int)ppt, (int)tiles)
     if (pool == 2) {
-        if (depth == 1) SLG_G2(1, 2, false);
-        else if (depth == 2) { if (pair) SLG_G2(2, 2, true); else SLG_G2(2, 2, false); }
-        else SLG_G2(3, 2, false);
+        if (depth == 1) SLG_G2(1, 2); else if (depth == 2) SLG_G2(2, 2); else SLG_G2(3, 2);
     } else {
-        if (depth == 1) SLG_G2(1, 1, false);
-        else if (depth == 2) { if (pair) SLG_G2(2, 1, true); else SLG_G2(2, 1, false); }
-        else SLG_G2(3, 1, false);
+        if (depth == 1) SLG_G2(1, 1); else if (depth == 2) SLG_G2(2, 1); else SLG_G2(3, 1);
     }
 #undef SLG_G2
     return true;

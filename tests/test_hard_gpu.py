@@ -409,11 +409,10 @@ def test_conv_gate_dispatch_kernel_equals_generic_tree_kernel(B):
         leaf = torch.randint(0, C * 9, (n, leaves), generator=g, dtype=torch.int32).to(dev)
         tt = torch.randint(0, 16, (n, leaves - 1), generator=g).to(dev)
         outs = []
-        for mode, pair in ((1, 0), (1, 1), (0, 0)):
-            assert L.slg_tuning_set(0, mode) == 0 and L.slg_tuning_set(3, pair) == 0
+        for mode in (1, 0):
+            assert L.slg_tuning_set(0, mode) == 0
             try:
                 outs.append(_hard.conv(x, leaf, tt, 2, depth, 3, 1, wr, pool))
             finally:
                 L.slg_tuning_set(0, 1)
-                L.slg_tuning_set(3, 0)
-        assert torch.equal(outs[0], outs[2]) and torch.equal(outs[1], outs[2]), (depth, pool, C, H, n, wr)
+        assert torch.equal(outs[0], outs[1]), (depth, pool, C, H, n, wr)
