@@ -134,10 +134,14 @@ fc_soft_bwd_kernel(const float4* __restrict__ x, int64_t nv, const int32_t* __re
 #pragma unroll
     for (int e = 0; e < AR * KT; ++e) acc_w[e] = 0.0f;
 
+    // small candidate sets keep the gathered inputs of the recompute in registers for the
+    // connection gradients instead of gathering them a second time
+    constexpr bool KEEP = AR * KT <= 16;
     for (int it = 0; it < FS_ITER; ++it) {
         const int64_t v = v0 + it * 32 + lane;
         if (v >= nv) break;
         float a[4][AR];
+        float4 xs[KEEP ? AR * KT : 1];
 #pragma unroll
         for (int j = 0; j < AR; ++j) {
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -146,6 +150,7 @@ fc_soft_bwd_kernel(const float4* __restrict__ x, int64_t nv, const int32_t* __re
                 if (k < K) {
                     const float wk = S.w[j * K + k];
                     const float4 xv = __ldg(&x[(int64_t)S.cand[j * K + k] * nv + v]);
+                    if constexpr (KEEP) xs[j * KT + k] = xv;
                     acc.x += wk * xv.x; acc.y += wk * xv.y; acc.z += wk * xv.z; acc.w += wk * xv.w;
                 }
             }
@@ -162,7 +167,9 @@ fc_soft_bwd_kernel(const float4* __restrict__ x, int64_t nv, const int32_t* __re
             for (int k = 0; k < KT; ++k) {
                 if (k >= K) break;
                 const int64_t row = S.cand[j * K + k];
-                const float4 xv = __ldg(&x[row * nv + v]);
+                float4 xv;
+                if constexpr (KEEP) xv = xs[j * KT + k];
+                else xv = __ldg(&x[row * nv + v]);
                 acc_w[j * KT + k] += ga[0][j] * xv.x + ga[1][j] * xv.y + ga[2][j] * xv.z + ga[3][j] * xv.w;
                 if (gx && S.w[j * K + k] != 0.0f) {
                     const float wk = S.w[j * K + k];
