@@ -9,6 +9,7 @@ import torch
 from .. import _hard
 from .plan import HardPlan, HardGraph
 from .convert import convert_logic_net, convert_logic_conv_net, convert_layer, convert_head
+from .artifact import save_packed, load_packed
 from .benchmark import (BenchResult, run_benchmark, run_conv_benchmark, print_report,
                         speedup_summary)
 from .packed import (BitpackedNet, BitpackedConvNet, BitpackedConvGPUNet, BitpackedGPULayer,
@@ -52,4 +53,5 @@ __all__ = ["convert_logic_net", "convert_logic_conv_net", "convert_layer", "conv
            "BitpackedConvGPULayer", "packed_unfold_gpu", "packed_or_pool_gpu",
            "pack_bits", "unpack_bits", "n_words", "HAS_TRITON", "BitpackedGroupSumHead",
            "BitpackedLearnedHead", "HardPlan", "HardGraph", "run_benchmark",
-           "run_conv_benchmark", "print_report", "speedup_summary", "BenchResult"]
+           "run_conv_benchmark", "print_report", "speedup_summary", "BenchResult",
+           "save_packed", "load_packed"]

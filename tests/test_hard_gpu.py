@@ -416,3 +416,16 @@ def test_conv_gate_dispatch_kernel_equals_generic_tree_kernel(B):
             finally:
                 L.slg_tuning_set(0, 1)
         assert torch.equal(outs[0], outs[1]), (depth, pool, C, H, n, wr)
+
+
+def test_loaded_packed_artefact_gives_the_same_counts(tmp_path):
+    import silogic_b200 as S
+    from silogic_b200.bitpacking import convert_logic_conv_net, save_packed, load_packed
+    torch.manual_seed(0)
+    m = S.LogicTreeNet(in_channels=6, in_hw=8, channels=[16, 32], head_widths=[80], tree_depth=2,
+                       node="gate16", tau=5.0, seed=0).to(dev)
+    bp = convert_logic_conv_net(m)
+    save_packed(bp, tmp_path / "net.npz")
+    back = load_packed(tmp_path / "net.npz", device=dev)
+    x = (np.random.default_rng(0).random((300, 6, 8, 8)) < 0.5).astype(np.uint8)
+    np.testing.assert_array_equal(back(x), bp(x))

@@ -126,3 +126,34 @@ def test_build_inverse_map_lists_every_reader_in_order():
     assert off.tolist() == [0, 2, 3, 4]
     assert list(zip(en.tolist(), el.tolist())) == [(0, 0), (1, 1), (1, 0), (0, 1)]
     assert edy.tolist() == [0, 1, 2, 1] and edx.tolist() == [1, 0, 0, 2]
+
+
+def test_packed_artefact_round_trip_and_corrupt_wiring(tmp_path):
+    """save_packed / load_packed keep every step's wiring, tables and geometry and the
+    head; a file whose wiring reads past its input is refused on load."""
+    import silogic_b200 as S
+    from silogic_b200.bitpacking import convert_logic_net, convert_logic_conv_net, save_packed, load_packed
+    torch.manual_seed(0)
+    for m, conv in ((S.LogicNet(30, 40, 2, node="walsh", connectome="topk", k=4, tau=3.0, seed=0), False),
+                    (S.LogicTreeNet(in_channels=3, in_hw=8, channels=[4, 8], head_widths=[40],
+                                    tree_depth=2, node="gate16", tau=2.0, seed=0), True)):
+        bp = convert_logic_conv_net(m) if conv else convert_logic_net(m)
+        path = tmp_path / ("c.npz" if conv else "f.npz")
+        save_packed(bp, path)
+        back = load_packed(path, device="cpu")
+        assert type(back).__name__ == type(bp).__name__
+        assert back.plan.in_shape == tuple(bp.plan.in_shape) and back.head.tau == bp.head.tau
+        for a, b in zip(bp.plan.steps, back.plan.steps):
+            assert a["op"] == b["op"]
+            key = "idx" if a["op"] == "fc" else "leaf"
+            assert torch.equal(a[key].to(torch.int32), b[key]) and torch.equal(a["tt"], b["tt"])
+    z = dict(np.load(tmp_path / "f.npz"))
+    z["step1/wiring"] = z["step1/wiring"].copy()
+    z["step1/wiring"][0, 0] = 40                     # layer 1 reads only 40 rows
+    np.savez(tmp_path / "bad.npz", **z)
+    with pytest.raises(IndexError):
+        load_packed(tmp_path / "bad.npz", device="cpu")
+    z["format"] = np.array("something else")
+    np.savez(tmp_path / "other.npz", **z)
+    with pytest.raises(ValueError):
+        load_packed(tmp_path / "other.npz", device="cpu")
