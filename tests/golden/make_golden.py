@@ -49,13 +49,17 @@ def _uniform(shape, seed):
 
 
 def _record(name, model, x, extra_pre=None, x_leaf=True, ctor=None, kwargs=None,
-            store=None, img_shape=None):
-    """Run hard + soft fwd/bwd on the reference and save an .npz fixture."""
+            store=None, img_shape=None, x_hard=None):
+    """Run hard + soft fwd/bwd on the reference and save an .npz fixture.  ``x_hard``:
+    a separate binary input for the hard path (fixtures with continuous soft inputs)."""
     import silogic  # noqa: F401  (reference)
-    store = {} if store is None else store
+    store = dict(store or {})
+    if x_hard is not None:
+        store["x_hard"] = x_hard.numpy()
     model.train()
     with torch.no_grad():
-        xin = extra_pre.forward_hard(x) if extra_pre is not None else x
+        xh = x if x_hard is None else x_hard
+        xin = extra_pre.forward_hard(xh) if extra_pre is not None else xh
         if extra_pre is not None:
             xin = _encoded_to_image(xin, img_shape)
         hard = model.forward_hard(xin)
@@ -199,9 +203,38 @@ def prim_cases():
     print("prims written")
 
 
+def continuous_conv_cases():
+    """Conv nets on continuous U[0,1] inputs: OR-pool windows then tie only at padding, so
+    the soft gradients pin the reference's own pool routing (binary inputs tie
+    everywhere).  The hard path gets the thresholded input ``x >= 0.5`` (``x_hard``)."""
+    from silogic.models import LogicTreeNet, LogicConvNet
+    cases = [
+        ("conv_cont_gate16_topk_d2", "LogicTreeNet",
+         dict(in_channels=6, in_hw=8, channels=[16, 32], head_widths=[80],
+              tree_depth=2, node="gate16", tau=20.0, seed=10)),
+        ("conv_cont_gate16_fixed_d3", "LogicConvNet",
+         dict(in_channels=6, in_hw=8, channels=[12, 24], head_widths=[60],
+              tree_depth=3, node="gate16", connect="fixed", tau=5.0, seed=11)),
+        ("conv_cont_walsh_k8_d2", "LogicConvNet",
+         dict(in_channels=6, in_hw=8, channels=[12, 20], head_widths=[100],
+              tree_depth=2, node="walsh", k=8, n_chan=2, tau=5.0, seed=12)),
+        ("conv_cont_multilinear_a3_d1", "LogicConvNet",
+         dict(in_channels=6, in_hw=8, channels=[12, 20], head_widths=[100],
+              tree_depth=1, node="multilinear", arity=3, k=4, tau=5.0, seed=13)),
+    ]
+    for i, (name, ctor, kw) in enumerate(cases):
+        torch.manual_seed(700 + i)
+        cls = {"LogicTreeNet": LogicTreeNet, "LogicConvNet": LogicConvNet}[ctor]
+        m = cls(**kw)
+        _randomise(m, 800 + i)
+        x = _uniform((40, 6, 8, 8), 900 + i)
+        _record(name, m, x, x_leaf=True, ctor=ctor, kwargs=kw, x_hard=(x >= 0.5).float())
+
+
 if __name__ == "__main__":
     if len(sys.argv) > 1:
         sys.path.insert(0, sys.argv[1])
     prim_cases()
     fc_cases()
     conv_cases()
+    continuous_conv_cases()

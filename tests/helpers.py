@@ -19,6 +19,14 @@ _conv = ["conv_gate16_topk_d2", "conv_gate16_fixed_d2", "conv_gate16_topk_d3_wir
 SEEDS.update({n: 100 + i for i, n in enumerate(_fc)})
 SEEDS.update({n: 400 + i for i, n in enumerate(_conv)})
 SEEDS["conv_multilinear_a6_enc"] = 450
+_cont = ["conv_cont_gate16_topk_d2", "conv_cont_gate16_fixed_d3", "conv_cont_walsh_k8_d2",
+         "conv_cont_multilinear_a3_d1"]
+SEEDS.update({n: 700 + i for i, n in enumerate(_cont)})
+
+
+def hard_input(z):
+    """The binary input of the hard path: ``x_hard`` where the soft input is continuous."""
+    return z["x_hard"] if "x_hard" in z.files else z["x"]
 
 
 def load(name):

@@ -3,7 +3,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import FIXTURES, build_model, encoder_image, load
+from helpers import FIXTURES, build_model, encoder_image, hard_input, load
 from oracle import hard as OH
 from oracle.spec import net_spec
 
@@ -14,7 +14,7 @@ dev = "cuda"
 @pytest.mark.parametrize("name", FIXTURES)
 def test_forward_hard_matches_reference_golden(name):
     m, enc, z, _ = build_model(name, dev)
-    x = torch.from_numpy(z["x"]).to(dev)
+    x = torch.from_numpy(hard_input(z)).to(dev)
     if enc is not None:
         x = encoder_image(enc.forward_hard(x), z)
     got = m.forward_hard(x)
@@ -25,7 +25,7 @@ def test_forward_hard_matches_reference_golden(name):
 def test_bitpacked_api_matches_reference_golden(name):
     from silogic_b200.bitpacking import convert_logic_net, convert_logic_conv_net
     m, enc, z, _ = build_model(name, dev)
-    x = torch.from_numpy(z["x"]).to(dev)
+    x = torch.from_numpy(hard_input(z)).to(dev)
     if enc is not None:
         x = encoder_image(enc.forward_hard(x), z)
     conv = "conv" in name

@@ -32,7 +32,7 @@ def _img(enc, shape, bits):
 def test_oracle_hard_counts_match_reference(case):
     ctor, kw, sd, z = load_fixture(os.path.join(GOLDEN, case + ".npz"))
     spec = net_spec(ctor, kw, sd)
-    x = z["x"]
+    x = z["x_hard"] if "x_hard" in z.files else z["x"]
     if "enc_kwargs" in z.files:
         bits, shape = _encode(z, x)
         e = H.learned_thermometer_bits(x, z["encsd/thresholds"])
