@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--config c1|c2|c3|c4|c5] [--extras c2,..|none] [--no-soft]
-                    [--no-cpu] [--reference-gpu] [--batch B]
+                    [--no-cpu] [--no-reference-gpu] [--batch B]
 
 Configs are BASELINE.json's (synthetic, seeded inputs; every parameter N(0,1)):
   c1  FC LogicNet 784 -> 8000 x 4, gate16, fixed wiring; hard + soft at B=1024
@@ -31,8 +31,8 @@ the first 128 samples with the CPU oracle; "cpu_baseline" times the reference's
 own CPU path (baseline/_ref) on a bounded sample of the same batch and says
 whether its counts equal the GPU's.
 --impl reference times the reference's own CPU path (rank 0 only) on a bounded
-sample per step; --reference-gpu adds the reference's Triton GPU path, timed in
-a child process, under "reference_gpu".
+sample per step.  At N=1 the reference's own GPU (Triton) path is also timed, in a
+child process, under "reference_gpu" (--no-reference-gpu skips it).
 """
 import argparse
 import json
@@ -579,6 +579,40 @@ def cpu_baseline(cfg_key, cfg, x_host, counts):
             "counts_equal_gpu": same}
 
 
+SOFT_CPU_SAMPLE = {"c1": 256, "c2": 64, "c3": 8, "c4": 2}
+
+
+def soft_cpu_baseline(cfg):
+    """The reference's soft training step on the host cores: ``model(x)`` and
+    ``.backward()`` through its own PyTorch path (baseline/_ref; its fused kernels need
+    CUDA, so the CPU path is the eager one), on a bounded batch of the config."""
+    silogic = import_reference()
+    if silogic is None:
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    key = [k for k, v in CONFIGS.items() if v is cfg or v["name"] == cfg["name"]][0]
+    n = SOFT_CPU_SAMPLE[key]
+    m, _, enc = reference_net(silogic, cfg)
+    m.train()
+    x = make_input(cfg, n, seed=100)
+    if cfg["inp"] == "bern":
+        x = x.float()
+    elif cfg["inp"] == "image":
+        from silogic.data import binarize_spatial
+        x = binarize_spatial(x, cfg["thresholds"]).float()
+    rmat = torch.randn(n, 10, generator=torch.Generator().manual_seed(5))
+
+    def step():
+        m.zero_grad()
+        (m(x) * rmat).sum().backward()
+    step()
+    t0 = time.perf_counter()
+    step()
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "samples/s", "cores": torch.get_num_threads(),
+            "kind": "reference", "sample": f"{n} samples, one model(x) + backward of the "
+            f"reference's PyTorch path (baseline/_ref) on the host, {dt:.2f} s"}
+
+
 def parity_check(cfg, x_host, counts, n=128):
     """Untimed: the GPU counts of the first ``n`` samples of the timed batch against the
     oracle (numpy restatement of the reference's bit-packed path)."""
@@ -728,8 +762,8 @@ def main():
                          "(default: c2 when the headline is c5; 'none' for none)")
     ap.add_argument("--no-soft", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--reference-gpu", action="store_true",
-                    help="also time the reference's Triton path (child process, N=1 only)")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip the reference's Triton path (timed in a child process, N=1 only)")
     ap.add_argument("--soft-only", action="store_true", help="profile the soft leg alone")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the hard batch (small cases for profiling)")
@@ -831,15 +865,21 @@ def main():
             line[e].update(workload=CONFIGS[e]["name"], batch_per_gpu=er["B"],
                            scaling=CONFIGS[e]["scaling"], unit="samples/s")
         if ws == 1 and not a.no_cpu:
+            for e, er in extra_res.items():
+                if "soft_fwd_bwd" in er:
+                    line[e]["soft_fwd_bwd"]["cpu_baseline"] = soft_cpu_baseline(CONFIGS[e])
             r = res["r"]
             line["cpu_baseline"] = cpu_baseline(a.config, cfg, r["x_first"], r["counts_first"])
             for e, er in extra_res.items():
                 line[e]["cpu_baseline"] = cpu_baseline(e, CONFIGS[e], er["r"]["x_first"],
                                                        er["r"]["counts_first"])
-        if ws == 1 and a.reference_gpu:
+        if ws == 1 and not a.no_reference_gpu and not a.batch:
+            keys = list(extra_res)
             del res, extra_res
             torch.cuda.empty_cache()
             line["reference_gpu"] = reference_gpu(a.config, 16384 if a.config == "c5" else 65536)
+            for e in keys:
+                line[e]["reference_gpu"] = reference_gpu(e, 16384 if e == "c5" else 65536)
         print(json.dumps(line))
     if ws > 1:
         torch.distributed.destroy_process_group()
