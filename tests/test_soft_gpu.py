@@ -18,9 +18,9 @@ FC = [n for n in FIXTURES if n.startswith("fc_")]
 CONV = [n for n in FIXTURES if n.startswith("conv_")]
 
 
-def assert_grad_close(got, ref, what):
+def assert_grad_close(got, ref, what, atol=1e-7):
     got = got.detach().cpu().numpy() if torch.is_tensor(got) else got
-    tol = 1e-5 * (np.abs(ref) + np.abs(ref).max()) + 1e-7
+    tol = 1e-5 * (np.abs(ref) + np.abs(ref).max()) + atol
     bad = np.abs(got - ref) > tol
     assert not bad.any(), f"{what}: {bad.sum()} of {bad.size} entries off, max err " \
                           f"{np.abs(got - ref).max():.3e} (ref max {np.abs(ref).max():.3e})"
@@ -86,12 +86,15 @@ def test_soft_matches_reference_golden(name):
         # binary inputs: pool windows tie, see the docstring
         _conv_grads_vs_oracle(name, m, enc, z, x)
         return
+    # conv nets: a deep block's gradient can be a near-total cancellation of O(1) terms
+    # (max |grad| ~1e-5 while the model's are ~1), so its fp32 noise is ~1e-7 absolute
+    atol = 1e-6 if name.startswith("conv_") else 1e-7
     for k in z.files:
         if k.startswith("grad/"):
             n = k[5:]
             got = x.grad if n == "x" else params[n].grad
             assert got is not None, n
-            assert_grad_close(got, z[k], f"{name} grad {n}")
+            assert_grad_close(got, z[k], f"{name} grad {n}", atol)
     if enc is not None:
         assert_grad_close(enc.thresholds.grad, z["encgrad/thresholds"], "encoder thresholds")
 
