@@ -691,7 +691,7 @@ def run_reference_gpu(cfg_key, cfg, a):
             h = h.reshape(-1, h.shape[-1]).contiguous()
             for gl in gnet.gpu_head_layers:
                 h = gl.forward(h)
-            return h"
+            return h
     for _ in range(warmup_n(a)):
         out = run()
     torch.cuda.synchronize()

@@ -19,7 +19,7 @@ _conv = ["conv_gate16_topk_d2", "conv_gate16_fixed_d2", "conv_gate16_topk_d3_wir
 SEEDS.update({n: 100 + i for i, n in enumerate(_fc)})
 SEEDS.update({n: 400 + i for i, n in enumerate(_conv)})
 SEEDS["conv_multilinear_a6_enc"] = 450
-_cont = ["conv_cont_gate16_topk_d2", "conv_cont_gate16_fixed_d3", "conv_cont_walsh_k8_d2",
+_cont = ["conv_cont_gate16_topk_d2", "conv_cont_gate16_fixed_d1", "conv_cont_walsh_k8_d2",
          "conv_cont_multilinear_a3_d1"]
 SEEDS.update({n: 700 + i for i, n in enumerate(_cont)})
 
