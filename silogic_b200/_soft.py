@@ -209,14 +209,18 @@ def _conv_meta(conv, wire_r=0, pool=1):
     if conv.stride != 1:
         raise NotImplementedError("soft conv kernels support stride 1")
     if conv.connect == "fixed":
-        cand = conv.leaf_idx.unsqueeze(-1).to(torch.int32).contiguous()
+        src = conv.leaf_idx
+        cand = src.unsqueeze(-1).to(torch.int32).contiguous()
         conn, K, ste = None, 1, 0
     else:
-        cand = conv.leaf_cand.to(torch.int32).contiguous()
+        src = conv.leaf_cand
+        cand = src.to(torch.int32).contiguous()
         conn, K, ste = conv.conn, conv.k, int(conv.gate_select == "hard")
     if K > 16:
         raise NotImplementedError("soft conv kernels support at most 16 candidates per leaf")
-    _hard.check_index_range(cand, conv.cin * conv.kh * conv.kw, "ConvLogicTree leaf candidates")
+    # checked on the module's own buffer (remembered until it changes), not on the
+    # per-call int32 copy, so a step replayed from a CUDA graph never re-checks
+    _hard.check_index_range(src, conv.cin * conv.kh * conv.kw, "ConvLogicTree leaf candidates")
     levels = conv.level_params()
     if kind == "gate16":
         params = torch.cat(list(levels), dim=1)                        # [n, nodes, 16]

@@ -341,3 +341,36 @@ def test_torch_compile_traces_the_custom_ops(ctor):
     torch.testing.assert_close(out, eager_out, rtol=1e-6, atol=1e-6)
     for p, r in zip(m.parameters(), ref):
         torch.testing.assert_close(p.grad, r, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("ctor", ["LogicNet", "LogicTreeNet"])
+def test_train_model_graphed_step_matches_eager(ctor):
+    """train_model's CUDA-graphed step (fwd + bwd + Adam, cosine learning rate) trains like
+    the eager step: the same data order gives parameters within rounding (gx atomics)
+    after two epochs.  The graphed step with on-device augmentation (bit flips, cutout)
+    runs as well."""
+    import silogic_b200 as S
+    from silogic_b200.train import train_model
+    g = torch.Generator().manual_seed(0)
+    if ctor == "LogicNet":
+        X = (torch.rand(1024, 64, generator=g) < 0.5).to(torch.uint8)
+        y = (X[:, :10].sum(1) > 5).long() * 3
+        make = lambda: S.LogicNet(64, 200, 2, node="walsh", connectome="topk", k=4, tau=3.0, seed=0)
+    else:
+        X = (torch.rand(512, 6, 8, 8, generator=g) < 0.5).to(torch.uint8)
+        y = (X[:, 0].sum((1, 2)) > 32).long() * 3
+        make = lambda: S.LogicTreeNet(in_channels=6, in_hw=8, channels=[16, 32], head_widths=[80],
+                                      tree_depth=2, node="gate16", tau=5.0, seed=0)
+    params = []
+    for graph in (True, False):
+        torch.manual_seed(1)
+        m = make()
+        res = train_model(m, X, y, X, y, dev, epochs=2, bs=128, lr=0.05, val_every=100,
+                          log=lambda *a: None, graph=graph, cosine=True)
+        params.append([p.detach().clone() for p in m.parameters()])
+        assert set(res) == {"test_soft", "test_hard", "train_min", "history"}
+    for a, b in zip(*params):
+        torch.testing.assert_close(a, b, rtol=1e-3, atol=1e-4)
+    res = train_model(make(), X, y, X, y, dev, epochs=1, bs=128, val_every=1,
+                      log=lambda *a: None, flip_p=0.05, cutout=3)
+    assert 0.0 <= res["test_hard"] <= 100.0 and res["history"]["epoch"] == [1]
