@@ -86,7 +86,7 @@ class GraphedTrainStep:
         self.opt.zero_grad(set_to_none=False)
         loss.backward()
         self.opt.step()
-        return loss
+        return loss.detach()        # keep no autograd graph alive between steps
 
     def step(self, xb, yb):
         self.x.copy_(xb, non_blocking=True)
@@ -166,6 +166,7 @@ def train_model(model, Xtr, ytr, Xte, yte, device, epochs=200, bs=256, lr=0.075,
                 opt.zero_grad()
                 loss.backward()
                 opt.step()
+                loss = loss.detach()
         if (ep + 1) % val_every == 0 or ep == epochs - 1:
             Xv = Xval if Xval is not None else Xte
             yv = yval if yval is not None else yte
