@@ -20,12 +20,6 @@
 namespace slg {
 
 constexpr int G2_THREADS = 256;
-#ifndef SLG_G2_PRELOAD
-#define SLG_G2_PRELOAD 1        // depth 2: load all four leaves before the first node
-#endif
-#ifndef SLG_G2_MINB
-#define SLG_G2_MINB 2           // minimum resident CTAs per SM requested from the compiler
-#endif
 
 // f(a, b) for the 4-bit table T, address a | b << 1 (slot 0 = the lower child), as a
 // single three-input logic op after constant folding.
@@ -129,8 +123,12 @@ __device__ __forceinline__ void eval_d2(const G2Ctx<4, POOL>& c, const uint32_t*
     node_apply(codes[2], r, d);
 }
 
-template <int DEPTH, int POOL>
-__global__ void __launch_bounds__(G2_THREADS, SLG_G2_MINB)
+// PRE: depth 2 loads all four leaves before the first node (16 loads in flight, 120
+// registers, 2 CTAs per SM) -- best on large images; otherwise leaves are loaded a pair
+// at a time and the compiler is held to 3 CTAs per SM -- best on small images, whose
+// CTAs have few positions to overlap load latency with.
+template <int DEPTH, int POOL, bool PRE>
+__global__ void __launch_bounds__(G2_THREADS, PRE ? 2 : 3)
 conv_gate2_kernel(const uint4* __restrict__ x, int H, int W, int nvec, const int32_t* __restrict__ leaf,
                   const uint64_t* __restrict__ tt, int kernel, int pad, int64_t n_out, int64_t wire_r,
                   int Hp, int Wp, uint4* __restrict__ out, int vt_shift, int slot_shift, int ppt,
@@ -198,7 +196,7 @@ conv_gate2_kernel(const uint4* __restrict__ x, int H, int W, int nvec, const int
         const int pn = (y0 * W + x0) * nvec;
         const bool inside = interior(y0, x0);
         uint32_t r[NWORD];
-        if constexpr (DEPTH == 2 && SLG_G2_PRELOAD) {
+        if constexpr (DEPTH == 2 && PRE) {
             if (inside) eval_d2<POOL, false>(c, codes, y0, x0, pn, r);
             else eval_d2<POOL, true>(c, codes, y0, x0, pn, r);
         } else {
@@ -241,7 +239,10 @@ bool launch_conv_gate2(const uint4* x, int64_t cin, int H, int W, int nvec, cons
     const int64_t tiles = cdiv(npos, slots * ppt);
     if (gy > 65535 || n_out * tiles > 0x7fffffffLL) return false;
     dim3 grid((unsigned)(n_out * tiles), (unsigned)gy);
-#define SLG_G2(D, P) conv_gate2_kernel<D, P><<<grid, G2_THREADS, 0, st>>>(x, H, W, nvec, leaf, tt, kernel, pad, n_out, wire_r, Hp, Wp, out, vs, ss, (int)ppt, (int)tiles)
+    // pooled positions per channel: <= 16 (C5's 8x8 and 4x4 blocks) takes the pairwise loads
+    const bool pre = npos > 16;
+#define SLG_G2(D, P) do { if (pre) conv_gate2_kernel<D, P, true><<<grid, G2_THREADS, 0, st>>>(x, H, W, nvec, leaf, tt, kernel, pad, n_out, wire_r, Hp, Wp, out, vs, ss, (int)ppt, (int)tiles); \
+                          else conv_gate2_kernel<D, P, false><<<grid, G2_THREADS, 0, st>>>(x, H, W, nvec, leaf, tt, kernel, pad, n_out, wire_r, Hp, Wp, out, vs, ss, (int)ppt, (int)tiles); } while (0)
     if (pool == 2) {
         if (depth == 1) SLG_G2(1, 2); else if (depth == 2) SLG_G2(2, 2); else SLG_G2(3, 2);
     } else {
