@@ -61,7 +61,7 @@ __device__ __forceinline__ void node_apply(uint32_t code, uint32_t (&a)[N], cons
 // Per-thread view of one output channel's leaves.
 template <int LEAVES, int POOL>
 struct G2Ctx {
-    const uint4* lp[LEAVES];     // channel plane of each leaf + this lane's vector
+    const uint4* lp[LEAVES];     // leaf tap at pixel (0, 0): plane + tap offset + lane's vector
     int ly[LEAVES], lx[LEAVES];  // tap offset (dy - pad, dx - pad)
     int dpn[LEAVES];             // the same offset in vectors: (ly * W + lx) * nvec
     int soff[POOL * POOL];       // offset of each pre-pool position of the window
@@ -79,7 +79,7 @@ __device__ __forceinline__ void load_leaf(const G2Ctx<LEAVES, POOL>& c, int l, i
         const int oy = s / POOL, ox = s % POOL;
         if (!CHECK || ((unsigned)(y0 + oy + c.ly[l]) < (unsigned)c.H &&
                        (unsigned)(x0 + ox + c.lx[l]) < (unsigned)c.W))
-            t = __ldg(c.lp[l] + (pn + c.dpn[l] + c.soff[s]));
+            t = __ldg(c.lp[l] + (pn + c.soff[s]));
         v[4 * s + 0] = t.x; v[4 * s + 1] = t.y; v[4 * s + 2] = t.z; v[4 * s + 3] = t.w;
     }
 }
@@ -176,10 +176,11 @@ conv_gate2_kernel(const uint4* __restrict__ x, int H, int W, int nvec, const int
         int ch, dy, dx;
         if (kernel == 3) { ch = r / 9; const int q = r - ch * 9; dy = q / 3; dx = q - dy * 3; }
         else { const int kk = kernel * kernel; ch = r / kk; const int q = r - ch * kk; dy = q / kernel; dx = q - dy * kernel; }
-        c.lp[l] = x + ch * plane + v0;
+        c.lp[l] = x + ch * plane + v0;     // the tap offset is added below
         c.ly[l] = dy - pad;
         c.lx[l] = dx - pad;
         c.dpn[l] = (c.ly[l] * W + c.lx[l]) * nvec;
+        c.lp[l] += c.dpn[l];              // only dereferenced where the tap is inside the image
     }
 #pragma unroll
     for (int s = 0; s < POOL * POOL; ++s) c.soff[s] = ((s / POOL) * W + (s % POOL)) * nvec;
