@@ -348,7 +348,9 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
             counts_all[c * chunk:c * chunk + n].copy_(graphs[n].replay())
             launches[0] += 2 if uses_chain(n) else 2 + len(plan.steps)
         if ws > 1 and collective:   # only the class counts leave the GPU
-            torch.distributed.all_gather_into_tensor(gathered, counts_all.to(wdt))
+            # bytes on the wire: neither NCCL nor gloo moves int16 itself
+            torch.distributed.all_gather_into_tensor(gathered.view(torch.uint8),
+                                                     counts_all.to(wdt).view(torch.uint8))
         return counts_all
 
     def step_e2e():
@@ -856,8 +858,9 @@ def main():
     if ws > 1:
         if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
             os.environ["NCCL_DEBUG"] = "WARN"      # keep stdout to the one JSON line
-        torch.distributed.init_process_group("nccl")
     torch.cuda.set_device(local)
+    if ws > 1:
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     if a.soft_only:
         soft = run_soft(cfg, cfg["soft_batch"], a.steps, warmup, rank, ws, dev)
