@@ -90,7 +90,14 @@ int slg_check_index_range(const int32_t* idx, int64_t count, int64_t limit, void
  *          generic LUT-tree kernel (0); both give identical bits;
  *   key 1  pooled positions per thread in that kernel (16);
  *   key 2  sorted near-uniform thermometer thresholds use the grid guess with two
- *          corrective comparisons (1) or a binary search (0); both give identical bits.
+ *          corrective comparisons (1) or a binary search (0); both give identical bits;
+ *   key 3  node form in the gate-dispatch kernel: one branch on the gate code per node
+ *          (0), three logic ops per word through constant masks with no branch (1), or
+ *          masks below the root and a branch at the root (2); identical bits;
+ *   key 4  arity-2 3x3 2x2-pooled blocks whose input planes fit one shared-memory
+ *          window with per-channel tables (227 KB: about 130 planes) can stage it and
+ *          evaluate every output channel from it: when the per-channel kernel would not
+ *          fill two waves (1), always (2), never (0); identical bits.
  * No counterpart in the reference (its Triton kernels take fixed block sizes). */
 int slg_tuning_set(int32_t key, int64_t value);
 

@@ -22,12 +22,18 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 int sm_count();
 
 // Process-wide tuning knobs (slg_tuning_set); defaults are the measured best.
-enum TuningKey { T_CONV_GATE2 = 0, T_CONV_PPT = 1, T_THERMO_GUESS = 2, T_NUM_KEYS = 3 };
+enum TuningKey { T_CONV_GATE2 = 0, T_CONV_PPT = 1, T_THERMO_GUESS = 2, T_CONV_NODE = 3, T_CONV_STAGE = 4, T_NUM_KEYS = 5 };
 int64_t tuning(int key);
 
 // Arity-2 conv tree blocks with uniform gate dispatch (conv_gate2.cu); false when the
 // shape is not one it handles (the caller then uses the generic LUT tree kernel).
 bool launch_conv_gate2(const uint4* x, int64_t cin, int H, int W, int nvec, const int32_t* leaf,
+                       const uint64_t* tt, int depth, int kernel, int pad, int64_t n_out,
+                       int64_t wire_r, int pool, int Hp, int Wp, uint4* out, cudaStream_t st);
+
+// Arity-2, 3x3, 2x2-pooled blocks whose input planes fit one shared-memory window
+// (conv_stage.cu); false when the shape is not one it handles.
+bool launch_conv_stage(const uint4* x, int64_t cin, int H, int W, int nvec, const int32_t* leaf,
                        const uint64_t* tt, int depth, int kernel, int pad, int64_t n_out,
                        int64_t wire_r, int pool, int Hp, int Wp, uint4* out, cudaStream_t st);
 

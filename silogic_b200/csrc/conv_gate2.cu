@@ -58,9 +58,33 @@ __device__ __forceinline__ void node_apply(uint32_t code, uint32_t (&a)[N], cons
     }
 }
 
+// The same node through its table as four all-ones / all-zero masks m[t] (t = a | b << 1):
+// a two-level bitwise multiplexer, three logic ops per word and no branch, so the loads of
+// the leaves and the nodes of a window share one basic block.
+template <int N>
+__device__ __forceinline__ void node_mux(const uint32_t (&m)[4], uint32_t (&a)[N], const uint32_t (&b)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const uint32_t lo = (a[i] & m[1]) | (~a[i] & m[0]);     // b = 0
+        const uint32_t hi = (a[i] & m[3]) | (~a[i] & m[2]);     // b = 1
+        a[i] = (b[i] & hi) | (~b[i] & lo);
+    }
+}
+
+// Node evaluation in the form MODE selects: 0 branch on the code; 1 masks; 2 masks below
+// the root and a branch at the root.
+template <int MODE, bool ROOT, int N>
+__device__ __forceinline__ void node_eval(uint32_t code, const uint32_t (&m)[4], uint32_t (&a)[N],
+                                          const uint32_t (&b)[N]) {
+    if constexpr (MODE == 0 || (MODE == 2 && ROOT)) node_apply(code, a, b);
+    else node_mux(m, a, b);
+}
+
 // Per-thread view of one output channel's leaves.
 template <int LEAVES, int POOL>
 struct G2Ctx {
+    uint32_t code[LEAVES - 1];   // node codes, level-major
+    uint32_t mk[LEAVES - 1][4];  // the same as masks
     const uint4* lp[LEAVES];     // leaf tap at pixel (0, 0): plane + tap offset + lane's vector
     int ly[LEAVES], lx[LEAVES];  // tap offset (dy - pad, dx - pad)
     int dpn[LEAVES];             // the same offset in vectors: (ly * W + lx) * nvec
@@ -87,47 +111,46 @@ __device__ __forceinline__ void load_leaf(const G2Ctx<LEAVES, POOL>& c, int l, i
 // Subtree of level LVL (0 = a leaf) with index i within its level, evaluated on every
 // word of the window: the two children first, then the node with one uniform branch.
 // Node ids are level-major (level 1 = the nodes over leaves), as in the tables array.
-template <int LVL, int LEAVES, int POOL, bool CHECK>
+template <int LVL, int LEAVES, int POOL, bool CHECK, int MODE>
 struct G2Sub {
-    static __device__ __forceinline__ void eval(const G2Ctx<LEAVES, POOL>& c, const uint32_t* codes,
-                                                int i, int y0, int x0, int pn,
-                                                uint32_t (&r)[POOL * POOL * 4]) {
+    static __device__ __forceinline__ void eval(const G2Ctx<LEAVES, POOL>& c, int i, int y0, int x0,
+                                                int pn, uint32_t (&r)[POOL * POOL * 4]) {
         uint32_t rb[POOL * POOL * 4];
-        G2Sub<LVL - 1, LEAVES, POOL, CHECK>::eval(c, codes, 2 * i, y0, x0, pn, r);
-        G2Sub<LVL - 1, LEAVES, POOL, CHECK>::eval(c, codes, 2 * i + 1, y0, x0, pn, rb);
+        G2Sub<LVL - 1, LEAVES, POOL, CHECK, MODE>::eval(c, 2 * i, y0, x0, pn, r);
+        G2Sub<LVL - 1, LEAVES, POOL, CHECK, MODE>::eval(c, 2 * i + 1, y0, x0, pn, rb);
         constexpr int base = LEAVES - (LEAVES >> (LVL - 1));   // nodes of lower levels
-        node_apply(codes[base + i], r, rb);
+        node_eval<MODE, (1 << LVL) == LEAVES>(c.code[base + i], c.mk[base + i], r, rb);
     }
 };
 
-template <int LEAVES, int POOL, bool CHECK>
-struct G2Sub<0, LEAVES, POOL, CHECK> {
-    static __device__ __forceinline__ void eval(const G2Ctx<LEAVES, POOL>& c, const uint32_t*, int i,
-                                                int y0, int x0, int pn, uint32_t (&r)[POOL * POOL * 4]) {
+template <int LEAVES, int POOL, bool CHECK, int MODE>
+struct G2Sub<0, LEAVES, POOL, CHECK, MODE> {
+    static __device__ __forceinline__ void eval(const G2Ctx<LEAVES, POOL>& c, int i, int y0, int x0,
+                                                int pn, uint32_t (&r)[POOL * POOL * 4]) {
         load_leaf<LEAVES, POOL, CHECK>(c, i, y0, x0, pn, r);
     }
 };
 
 // Depth 2 (the LogicTreeNet block): all four leaves are loaded before any node is
 // evaluated, so 16 loads per thread are in flight at once.
-template <int POOL, bool CHECK>
-__device__ __forceinline__ void eval_d2(const G2Ctx<4, POOL>& c, const uint32_t* codes, int y0, int x0,
-                                        int pn, uint32_t (&r)[POOL * POOL * 4]) {
+template <int POOL, bool CHECK, int MODE>
+__device__ __forceinline__ void eval_d2(const G2Ctx<4, POOL>& c, int y0, int x0, int pn,
+                                        uint32_t (&r)[POOL * POOL * 4]) {
     uint32_t b[POOL * POOL * 4], d[POOL * POOL * 4], e[POOL * POOL * 4];
     load_leaf<4, POOL, CHECK>(c, 0, y0, x0, pn, r);
     load_leaf<4, POOL, CHECK>(c, 1, y0, x0, pn, b);
     load_leaf<4, POOL, CHECK>(c, 2, y0, x0, pn, d);
     load_leaf<4, POOL, CHECK>(c, 3, y0, x0, pn, e);
-    node_apply(codes[0], r, b);
-    node_apply(codes[1], d, e);
-    node_apply(codes[2], r, d);
+    node_eval<MODE, false>(c.code[0], c.mk[0], r, b);
+    node_eval<MODE, false>(c.code[1], c.mk[1], d, e);
+    node_eval<MODE, true>(c.code[2], c.mk[2], r, d);
 }
 
 // PRE: depth 2 loads all four leaves before the first node (16 loads in flight, 120
 // registers, 2 CTAs per SM) -- best on large images; otherwise leaves are loaded a pair
 // at a time and the compiler is held to 3 CTAs per SM -- best on small images, whose
 // CTAs have few positions to overlap load latency with.
-template <int DEPTH, int POOL, bool PRE>
+template <int DEPTH, int POOL, bool PRE, int MODE>
 __global__ void __launch_bounds__(G2_THREADS, PRE ? 2 : 3)
 conv_gate2_kernel(const uint4* __restrict__ x, int H, int W, int nvec, const int32_t* __restrict__ leaf,
                   const uint64_t* __restrict__ tt, int kernel, int pad, int64_t n_out, int64_t wire_r,
@@ -184,9 +207,12 @@ conv_gate2_kernel(const uint4* __restrict__ x, int H, int W, int nvec, const int
     }
 #pragma unroll
     for (int s = 0; s < POOL * POOL; ++s) c.soff[s] = ((s / POOL) * W + (s % POOL)) * nvec;
-    uint32_t codes[NODES];
 #pragma unroll
-    for (int i = 0; i < NODES; ++i) codes[i] = (uint32_t)__ldg(&tt[n * NODES + i]) & 15u;
+    for (int i = 0; i < NODES; ++i) {
+        c.code[i] = (uint32_t)__ldg(&tt[n * NODES + i]) & 15u;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) c.mk[i][t] = 0u - ((c.code[i] >> t) & 1u);
+    }
 
     auto interior = [&](int y0, int x0) {
         return y0 - pad >= 0 && y0 + POOL - 1 + kernel - 1 - pad < H &&
@@ -198,11 +224,11 @@ conv_gate2_kernel(const uint4* __restrict__ x, int H, int W, int nvec, const int
         const bool inside = interior(y0, x0);
         uint32_t r[NWORD];
         if constexpr (DEPTH == 2 && PRE) {
-            if (inside) eval_d2<POOL, false>(c, codes, y0, x0, pn, r);
-            else eval_d2<POOL, true>(c, codes, y0, x0, pn, r);
+            if (inside) eval_d2<POOL, false, MODE>(c, y0, x0, pn, r);
+            else eval_d2<POOL, true, MODE>(c, y0, x0, pn, r);
         } else {
-            if (inside) G2Sub<DEPTH, LEAVES, POOL, false>::eval(c, codes, 0, y0, x0, pn, r);
-            else G2Sub<DEPTH, LEAVES, POOL, true>::eval(c, codes, 0, y0, x0, pn, r);
+            if (inside) G2Sub<DEPTH, LEAVES, POOL, false, MODE>::eval(c, 0, y0, x0, pn, r);
+            else G2Sub<DEPTH, LEAVES, POOL, true, MODE>::eval(c, 0, y0, x0, pn, r);
         }
         uint4 acc = make_uint4(r[0], r[1], r[2], r[3]);
 #pragma unroll
@@ -242,14 +268,18 @@ bool launch_conv_gate2(const uint4* x, int64_t cin, int H, int W, int nvec, cons
     dim3 grid((unsigned)(n_out * tiles), (unsigned)gy);
     // pooled positions per channel: <= 16 (C5's 8x8 and 4x4 blocks) takes the pairwise loads
     const bool pre = npos > 16;
-#define SLG_G2(D, P) do { if (pre) conv_gate2_kernel<D, P, true><<<grid, G2_THREADS, 0, st>>>(x, H, W, nvec, leaf, tt, kernel, pad, n_out, wire_r, Hp, Wp, out, vs, ss, (int)ppt, (int)tiles); \
-                          else conv_gate2_kernel<D, P, false><<<grid, G2_THREADS, 0, st>>>(x, H, W, nvec, leaf, tt, kernel, pad, n_out, wire_r, Hp, Wp, out, vs, ss, (int)ppt, (int)tiles); } while (0)
+    const int mode = (int)tuning(T_CONV_NODE);
+#define SLG_G2M(D, P, PR, M) conv_gate2_kernel<D, P, PR, M><<<grid, G2_THREADS, 0, st>>>(x, H, W, nvec, leaf, tt, kernel, pad, n_out, wire_r, Hp, Wp, out, vs, ss, (int)ppt, (int)tiles)
+#define SLG_G2P(D, P, PR) do { if (mode == 1) SLG_G2M(D, P, PR, 1); else if (mode == 2) SLG_G2M(D, P, PR, 2); else SLG_G2M(D, P, PR, 0); } while (0)
+#define SLG_G2(D, P) do { if (pre) SLG_G2P(D, P, true); else SLG_G2P(D, P, false); } while (0)
     if (pool == 2) {
         if (depth == 1) SLG_G2(1, 2); else if (depth == 2) SLG_G2(2, 2); else SLG_G2(3, 2);
     } else {
         if (depth == 1) SLG_G2(1, 1); else if (depth == 2) SLG_G2(2, 1); else SLG_G2(3, 1);
     }
 #undef SLG_G2
+#undef SLG_G2P
+#undef SLG_G2M
     return true;
 }
 

@@ -452,6 +452,9 @@ extern "C" int slg_conv_hard(const uint64_t* x, int64_t cin, int64_t H, int64_t 
     auto xs = reinterpret_cast<const uint4*>(x);
     auto os = reinterpret_cast<uint4*>(out);
     cudaStream_t st = as_stream(stream);
+    if (arity == 2 && launch_conv_stage(xs, cin, (int)H, (int)W, (int)nvec, leaf, tt, depth, kernel, pad,
+                                        n_out, wire_r, pool, (int)Hp, (int)Wp, os, st))
+        return check_launch("slg_conv_hard");
     if (arity == 2 && launch_conv_gate2(xs, cin, (int)H, (int)W, (int)nvec, leaf, tt, depth, kernel, pad,
                                         n_out, wire_r, pool, (int)Hp, (int)Wp, os, st))
         return check_launch("slg_conv_hard");

@@ -394,28 +394,41 @@ def test_thermometer_pack_exact_at_threshold_boundaries(thr):
     assert not got[:, ref.shape[1]:].any(), "padding words must be zero"
 
 
+# (key 0 gate dispatch, key 4 staged window: 1 below its size cut-over, 2 always, key 3
+# node form): every conv path for arity-2 trees, the first entry being the default
+CONV_PATHS = [(1, 1, 0), (1, 2, 0), (1, 2, 1), (1, 0, 0), (1, 0, 1), (1, 0, 2), (0, 0, 0)]
+
+
 @pytest.mark.parametrize("B", [100, 4096])
 def test_conv_gate_dispatch_kernel_equals_generic_tree_kernel(B):
-    """The arity-2 gate-dispatch conv kernel and the generic LUT-tree kernel give the
-    same bits (depths 1-3, pool 1 and 2, wire residual, image sizes down to 2x2)."""
+    """The arity-2 conv kernels -- the staged shared-memory window, the gate-dispatch
+    kernel with each node form, and the generic LUT-tree kernel -- give the same bits
+    (depths 1-3, pool 1 and 2, pad 0 and 1, wire residual, image sizes down to 2x2,
+    odd sizes, near the staged kernel's shared-memory limit and past it)."""
     from silogic_b200 import _hard, _lib
     L = _lib.lib()
     g = torch.Generator().manual_seed(B)
-    for depth, pool, C, H, n, wr in [(1, 2, 5, 9, 7, 0), (2, 2, 15, 32, 40, 0), (3, 1, 4, 6, 9, 0),
-                                     (2, 2, 16, 4, 24, 8), (2, 2, 8, 2, 300, 0)]:
+    cases = [(1, 2, 5, 9, 7, 0, 1), (2, 2, 15, 32, 40, 0, 1), (3, 1, 4, 6, 9, 0, 1),
+             (2, 2, 16, 4, 24, 8, 1), (2, 2, 8, 2, 300, 0, 1), (2, 2, 6, 11, 33, 0, 0),
+             (3, 2, 7, 13, 20, 3, 1), (2, 2, 118, 10, 70, 0, 1), (2, 2, 134, 6, 30, 0, 1),
+             (2, 2, 9, 19, 17, 2, 0)]
+    for depth, pool, C, H, n, wr, pad in cases:
         ldw = _hard.ldw_for(B)
         x = torch.randint(-2**62, 2**62, (C, H, H, ldw), generator=g).to(dev)
         leaves = 2 ** depth
         leaf = torch.randint(0, C * 9, (n, leaves), generator=g, dtype=torch.int32).to(dev)
         tt = torch.randint(0, 16, (n, leaves - 1), generator=g).to(dev)
         outs = []
-        for mode in (1, 0):
-            assert L.slg_tuning_set(0, mode) == 0
+        for k0, k4, k3 in CONV_PATHS:
+            assert L.slg_tuning_set(0, k0) == 0 and L.slg_tuning_set(4, k4) == 0
+            assert L.slg_tuning_set(3, k3) == 0
             try:
-                outs.append(_hard.conv(x, leaf, tt, 2, depth, 3, 1, wr, pool))
+                outs.append(_hard.conv(x, leaf, tt, 2, depth, 3, pad, wr, pool))
             finally:
-                L.slg_tuning_set(0, 1)
-        assert torch.equal(outs[0], outs[1]), (depth, pool, C, H, n, wr)
+                for key, val in ((0, 1), (4, 1), (3, 0)):
+                    L.slg_tuning_set(key, val)
+        for (k0, k4, k3), o in zip(CONV_PATHS[1:], outs[1:]):
+            assert torch.equal(outs[0], o), (depth, pool, C, H, n, wr, pad, k0, k4, k3)
 
 
 def test_loaded_packed_artefact_gives_the_same_counts(tmp_path):
