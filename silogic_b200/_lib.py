@@ -90,8 +90,22 @@ def lib():
             fn.restype = res
         L.slg_last_error.restype = ctypes.c_char_p
         L.slg_last_error.argtypes = []
+        _apply_env_tuning(L)
         _lib = L
     return _lib
+
+
+def _apply_env_tuning(L):
+    """SLG_TUNING="key=value,..." sets ``slg_tuning_set`` knobs when the library loads
+    (kernel variants; results are identical for every setting)."""
+    spec = os.environ.get("SLG_TUNING", "").strip()
+    for item in filter(None, (t.strip() for t in spec.split(","))):
+        try:
+            key, val = (int(v) for v in item.split("="))
+        except ValueError:
+            raise SilogicError(f"SLG_TUNING: bad item {item!r} (want key=value)") from None
+        if L.slg_tuning_set(key, val) != 0:
+            raise SilogicError(f"SLG_TUNING: {L.slg_last_error().decode()}")
 
 
 def declare(name, argtypes):

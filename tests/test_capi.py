@@ -128,3 +128,28 @@ def test_plan_and_layers_reject_out_of_range_wiring():
     with pytest.raises(IndexError):
         PackedConvLayer(torch.tensor([[0, 27]], dtype=torch.int32), torch.tensor([[6]]), 2, 1, 3,
                         1, 3, 1)
+
+
+def test_tuning_keys_and_env():
+    """slg_tuning_set accepts each key's documented range and refuses the rest;
+    SLG_TUNING applies settings when the library loads and rejects bad ones."""
+    import subprocess
+    import sys
+    L = _lib.lib()
+    ranges = {0: (0, 1), 1: (1, 64), 2: (0, 1), 3: (0, 2), 4: (0, 2)}
+    defaults = {0: 1, 1: 16, 2: 1, 3: 0, 4: 1}
+    try:
+        for key, (lo, hi) in ranges.items():
+            assert L.slg_tuning_set(key, lo) == 0 and L.slg_tuning_set(key, hi) == 0
+            assert L.slg_tuning_set(key, lo - 1) != 0 and L.slg_tuning_set(key, hi + 1) != 0
+        assert L.slg_tuning_set(5, 0) != 0 and L.slg_tuning_set(-1, 0) != 0
+    finally:
+        for key, val in defaults.items():
+            L.slg_tuning_set(key, val)
+    code = "import silogic_b200._lib as l; l.lib()"
+    env = dict(os.environ, SLG_TUNING="4=2, 3=1")
+    assert subprocess.run([sys.executable, "-c", code], env=env, cwd=ROOT).returncode == 0
+    for bad in ("4=9", "4", "x=1"):
+        env["SLG_TUNING"] = bad
+        r = subprocess.run([sys.executable, "-c", code], env=env, cwd=ROOT, capture_output=True, text=True)
+        assert r.returncode != 0 and "SLG_TUNING" in r.stderr
