@@ -114,11 +114,18 @@ def build_model(cfg, seed=0):
 
 
 def make_input(cfg, B, seed):
-    """Synthetic batch: Bernoulli(0.3) features (uint8) or U[0,1] 3x32x32 pixels (fp32)."""
+    """Synthetic batch: Bernoulli(0.3) features (uint8), or uniform 3x32x32 uint8 pixels,
+    the form CIFAR images are stored in; pixel k stands for the fp32 value k / 255 that
+    torchvision's ToTensor gives (``image_float``)."""
     g = torch.Generator().manual_seed(seed)
     if cfg["inp"] == "bern":
         return (torch.rand(B, cfg["kwargs"]["in_dim"], generator=g) < 0.3).to(torch.uint8)
-    return torch.rand(B, 3, 32, 32, generator=g)
+    return torch.randint(0, 256, (B, 3, 32, 32), generator=g, dtype=torch.uint8)
+
+
+def image_float(x):
+    """uint8 pixels -> the fp32 images k / 255 (ToTensor) that float-input paths take."""
+    return x.float() / 255 if x.dtype == torch.uint8 else x
 
 
 class ClockSampler:
@@ -215,7 +222,7 @@ def events():
 def hard_stage_bytes(cfg, plan):
     """Layer-wise algorithmic bytes PER SAMPLE of each hard stage: every stage reads its
     input bits once and writes its output bits once; the first stage reads the raw
-    input (uint8 features, or fp32 pixels for the image configs)."""
+    input (uint8 features, or uint8 pixels for the image configs)."""
     out = []
     if cfg["inp"] == "bern":
         F = cfg["kwargs"]["in_dim"]
@@ -223,7 +230,7 @@ def hard_stage_bytes(cfg, plan):
         bits = F
     else:
         T = len(cfg["thresholds"]) if cfg["inp"] == "image" else cfg["bits"]
-        out.append(("pack", 3 * 32 * 32 * 4 + 3 * T * 32 * 32 / 8))
+        out.append(("pack", 3 * 32 * 32 + 3 * T * 32 * 32 / 8))
         bits, hw = 3 * T * 32 * 32, 32
     for st in plan.steps:
         if st["op"] == "fc":
@@ -439,9 +446,9 @@ def run_soft(cfg, B, steps, warmup, rank, ws, dev):
     if cfg["inp"] == "bern":
         x = x.float()
     elif cfg["inp"] == "image":
-        x = S.binarize_spatial(x, cfg["thresholds"]).float()
+        x = S.binarize_spatial(image_float(x), cfg["thresholds"]).float()
     else:
-        x = x.reshape(B, -1)
+        x = image_float(x).reshape(B, -1)
     rmat = torch.randn(B, 10, generator=torch.Generator().manual_seed(5)).to(dev)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.int32, device=dev)
     params = list(model.parameters()) + (list(enc.parameters()) if enc is not None else [])
@@ -524,10 +531,10 @@ def reference_cpu_step(silogic, cfg, bp, enc, x):
         xb = x.numpy()
     elif cfg["inp"] == "image":
         from silogic.data import binarize_spatial
-        xb = binarize_spatial(x, cfg["thresholds"]).numpy()
+        xb = binarize_spatial(image_float(x), cfg["thresholds"]).numpy()
     else:
         n = x.shape[0]
-        e = enc.forward_hard(x.reshape(n, -1))
+        e = enc.forward_hard(image_float(x).reshape(n, -1))
         xb = e.view(n, 3, 32, 32, cfg["bits"]).permute(0, 1, 4, 2, 3).reshape(n, -1, 32, 32).numpy()
     return np.rint(bp(xb) * cfg["kwargs"]["tau"]).astype(np.int64)
 
@@ -541,7 +548,7 @@ def cpu_port_sample(cfg, x):
     sd = {k: v.numpy() for k, v in model.state_dict().items()}
     spec = net_spec(cfg["ctor"], cfg["kwargs"], sd)
     n = x.shape[0]
-    xn = x.numpy()
+    xn = x.numpy() if cfg["inp"] == "bern" else image_float(x).numpy()
     if cfg["inp"] == "image":
         xn = OH.thermometer_bits(xn, cfg["thresholds"])
     elif cfg["inp"] == "encoder":
@@ -601,7 +608,9 @@ def soft_cpu_baseline(cfg):
         x = x.float()
     elif cfg["inp"] == "image":
         from silogic.data import binarize_spatial
-        x = binarize_spatial(x, cfg["thresholds"]).float()
+        x = binarize_spatial(image_float(x), cfg["thresholds"]).float()
+    else:
+        x = image_float(x)
     rmat = torch.randn(n, 10, generator=torch.Generator().manual_seed(5))
 
     def step():
@@ -676,7 +685,7 @@ def run_reference_gpu(cfg_key, cfg, a):
         from silogic.bitpacking.packed_layer import pack_conv_input
         from silogic.bitpacking.ops import n_words
         from silogic.data import binarize_spatial
-        xb = binarize_spatial(x, cfg["thresholds"]).numpy()
+        xb = binarize_spatial(image_float(x), cfg["thresholds"]).numpy()
         gnet = BitpackedConvGPUNet.from_conv_net(bp, 32, 32, "cuda")
         run = lambda: gnet(xb)
         what = "BitpackedConvGPUNet (Triton gate trees, torch unfold/OR-pool) + host pack/head"
@@ -886,6 +895,9 @@ def main():
             "higher_is_better": True, "scaling": cfg["scaling"], "vs_baseline": None,
             "dtype": "u64", "data": "synthetic (seeded inputs, N(0,1) parameters)",
             "config": {"workload": cfg["name"], "batch_per_gpu": res["B"],
+                       "input": ("seeded uint8 3x32x32 pixels, pixel k = fp32 k/255 (ToTensor); the "
+                                 "reference arms take the same images as fp32"
+                                 if cfg["inp"] != "bern" else "seeded Bernoulli(0.3) uint8 features"),
                        "global_batch": res["total"],
                        "parallelism": f"batch shard x{ws}, counts all-gathered (int16 on the wire)",
                        "l2": "flushed before each step (256 MB write, then read back so L2 is clean)",

@@ -71,6 +71,12 @@ int slg_unpack_u8(const uint64_t* p, int64_t F, int64_t ldw, int64_t B, uint8_t*
 int slg_thermo_pack(const float* x, int64_t B, int64_t C, int64_t HW, const float* thr,
                     int64_t T, int32_t mode, uint64_t* out, int64_t ldw, void* stream);
 
+/* The same from uint8 pixels [B, C, HW]: pixel k is read as the fp32 quotient k / 255
+ * (round to nearest, the value torchvision's ToTensor gives), so the bits equal
+ * slg_thermo_pack of that float image; a quarter of the input bytes. */
+int slg_thermo_pack_u8(const uint8_t* x, int64_t B, int64_t C, int64_t HW, const float* thr,
+                       int64_t T, int32_t mode, uint64_t* out, int64_t ldw, void* stream);
+
 /* ----------------------------------------------------------- hard circuit */
 
 /* Validate gather indices before they reach a kernel: every idx[i] (i < count) must

@@ -76,7 +76,9 @@ def _thresholds(thresholds, device):
 
 
 def thermo_pack(img, thresholds, mode=0, ldw=None):
-    """Thermometer-encode ``[B, C, H, W]`` fp32 and pack to ``[C*T, H, W, ldw]``.
+    """Thermometer-encode ``[B, C, H, W]`` fp32 -- or uint8, pixel k read as the fp32
+    quotient k / 255 as torchvision's ``ToTensor`` gives it -- and pack to
+    ``[C*T, H, W, ldw]``.
 
     mode 0 = ``binarize_spatial`` (shared thresholds, channel ``t*C + c``; a sorted
     Python sequence takes the binary-search kernel path);
@@ -93,10 +95,15 @@ def thermo_pack(img, thresholds, mode=0, ldw=None):
     T = thr.shape[-1] if thr.dim() else 1
     ldw = ldw or ldw_for(B)
     out = torch.empty((C * T, H, W, ldw), dtype=torch.int64, device=img.device)
-    x = img.float().contiguous()
     mode = int(mode)
-    call("slg_thermo_pack", ptr(x), B, C, H * W, ptr(thr), T, mode, ptr(out), ldw,
-         stream_ptr(img.device))
+    if img.dtype == torch.uint8:    # pixel k read as k / 255 (ToTensor), a quarter of the bytes
+        x = img.contiguous()
+        call("slg_thermo_pack_u8", ptr(x), B, C, H * W, ptr(thr), T, mode, ptr(out), ldw,
+             stream_ptr(img.device))
+    else:
+        x = img.float().contiguous()
+        call("slg_thermo_pack", ptr(x), B, C, H * W, ptr(thr), T, mode, ptr(out), ldw,
+             stream_ptr(img.device))
     return out
 
 

@@ -27,6 +27,7 @@ _SIGS = {
     "slg_pack_f32": [_p, _i64, _i64, _p, _i64, _p],
     "slg_unpack_u8": [_p, _i64, _i64, _i64, _p, _p],
     "slg_thermo_pack": [_p, _i64, _i64, _i64, _p, _i64, _i32, _p, _i64, _p],
+    "slg_thermo_pack_u8": [_p, _i64, _i64, _i64, _p, _i64, _i32, _p, _i64, _p],
     "slg_fc_hard": [_p, _i64, _i64, _p, _p, _i32, _i64, _i64, _p, _p],
     "slg_conv_hard": [_p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _i64, _i64,
                       _i32, _p, _p],

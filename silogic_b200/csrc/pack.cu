@@ -168,9 +168,31 @@ constexpr int TH_S = 256;
 // LOG > 0: shared thresholds sorted ascending, searched in LOG fixed steps over the
 // chunk padded with +inf (count of thresholds <= v, then a thermometer mask);
 // LOG == 0: one comparison per threshold (unsorted shared, or learned per feature).
-template <int LOG>
+// Pixel loads of the tile: fp32 as given, or uint8 k read as k / 255 rounded to fp32 (the
+// value torchvision's ToTensor gives), through a per-CTA table of the 256 quotients.
+template <typename TIn>
+struct ThermoIn;
+
+template <>
+struct ThermoIn<float> {
+    static constexpr int VEC = 4;                      // pixels per 16-byte load
+    __device__ __forceinline__ void init() {}
+    __device__ __forceinline__ float operator()(float v) const { return v; }
+};
+
+template <>
+struct ThermoIn<uint8_t> {
+    static constexpr int VEC = 16;
+    float* q;                                          // shared table [256]
+    __device__ __forceinline__ void init() {
+        if (threadIdx.x < 256) q[threadIdx.x] = __fdiv_rn((float)threadIdx.x, 255.0f);
+    }
+    __device__ __forceinline__ float operator()(uint8_t v) const { return q[v]; }
+};
+
+template <int LOG, typename TIn>
 __global__ void __launch_bounds__(256)
-thermo_kernel(const float* __restrict__ x, int64_t B, int64_t C, int64_t HW,
+thermo_kernel(const TIn* __restrict__ x, int64_t B, int64_t C, int64_t HW,
               const float* __restrict__ thr, int T, int mode,
               uint64_t* __restrict__ out, int64_t ldw, int use_guess) {
     __shared__ float tile[TH_S][TH_FT + 1];
@@ -179,40 +201,49 @@ thermo_kernel(const float* __restrict__ x, int64_t B, int64_t C, int64_t HW,
     __shared__ float s_pad[34];            // NaN, the sorted chunk, NaN (guess-and-correct)
     __shared__ int64_t s_row[TH_FT];       // pixel p of each feature
     __shared__ int32_t s_c[TH_FT];         // channel c of each feature
+    __shared__ float s_q[256];             // uint8 input: k / 255
+    ThermoIn<TIn> cvt;
+    if constexpr (sizeof(TIn) == 1) cvt.q = s_q;
+    cvt.init();
     const int64_t F = C * HW;
     const int64_t f0 = (int64_t)blockIdx.x * TH_FT;
     const int64_t w0 = (int64_t)blockIdx.y * 4;
     const int64_t b0 = w0 * 64;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const bool vec = (F % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+    constexpr int VEC = ThermoIn<TIn>::VEC;
+    const bool vec = (F % VEC == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
     if (threadIdx.x < TH_FT) {
         const int64_t ff = f0 + threadIdx.x;
         const int64_t c = ff / HW, p = ff - c * HW;
         s_c[threadIdx.x] = (int32_t)c;
         s_row[threadIdx.x] = p;
     }
+    if constexpr (sizeof(TIn) == 1) __syncthreads();   // the quotient table
     if (vec && f0 + TH_FT <= F) {
-        // all 8 16-byte loads of this thread in flight before the shared stores
-        constexpr int N = TH_S * (TH_FT / 4) / 256;
-        float4 r[N];
+        // all 16-byte loads of this thread in flight before the shared stores
+        constexpr int PER = TH_FT / VEC;                // loads per tile row
+        constexpr int N = TH_S * PER / 256;
+        uint4 r[N];
 #pragma unroll
         for (int k = 0; k < N; ++k) {
             const int i = threadIdx.x + 256 * k;
-            const int64_t b = b0 + i / (TH_FT / 4);
-            r[k] = b < B ? __ldg(reinterpret_cast<const float4*>(x + b * F + f0 + (i % (TH_FT / 4)) * 4))
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
+            const int64_t b = b0 + i / PER;
+            r[k] = b < B ? __ldg(reinterpret_cast<const uint4*>(x + b * F + f0 + (i % PER) * VEC))
+                         : make_uint4(0u, 0u, 0u, 0u);
         }
 #pragma unroll
         for (int k = 0; k < N; ++k) {
             const int i = threadIdx.x + 256 * k;
-            const int sr = i / (TH_FT / 4), q = (i % (TH_FT / 4)) * 4;
-            tile[sr][q] = r[k].x; tile[sr][q + 1] = r[k].y; tile[sr][q + 2] = r[k].z; tile[sr][q + 3] = r[k].w;
+            const int sr = i / PER, q = (i % PER) * VEC;
+            const TIn* e = reinterpret_cast<const TIn*>(&r[k]);
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) tile[sr][q + j] = cvt(e[j]);
         }
     } else {
         for (int i = threadIdx.x; i < TH_S * TH_FT; i += 256) {
             const int sr = i / TH_FT, f = i % TH_FT;
             const int64_t b = b0 + sr, ff = f0 + f;
-            tile[sr][f] = (b < B && ff < F) ? x[b * F + ff] : 0.0f;
+            tile[sr][f] = (b < B && ff < F) ? cvt(x[b * F + ff]) : 0.0f;
         }
     }
     const int nf = (int)min((int64_t)TH_FT, F - f0);
@@ -410,15 +441,16 @@ extern "C" int slg_unpack_u8(const uint64_t* p, int64_t F, int64_t ldw, int64_t 
     return check_launch("slg_unpack_u8");
 }
 
-extern "C" int slg_thermo_pack(const float* x, int64_t B, int64_t C, int64_t HW, const float* thr,
-                               int64_t T, int32_t mode, uint64_t* out, int64_t ldw, void* stream) {
+template <typename TIn>
+static int thermo_pack(const char* what, const TIn* x, int64_t B, int64_t C, int64_t HW, const float* thr,
+                       int64_t T, int32_t mode, uint64_t* out, int64_t ldw, void* stream) {
     if (B < 0 || C <= 0 || HW <= 0 || T <= 0 || mode < 0 || mode > 2)
-        return set_error(SLG_ERR_ARG, "slg_thermo_pack: bad arguments");
+        return set_error(SLG_ERR_ARG, "%s: bad arguments", what);
     if (B == 0) return SLG_OK;
     int64_t nw = cdiv(B, 64);
-    if (ldw < nw) return set_error(SLG_ERR_ARG, "slg_thermo_pack: ldw too small");
-    if (!x || !thr || !out) return set_error(SLG_ERR_ARG, "slg_thermo_pack: null pointer");
-    if (cdiv(ldw, 4) > 65535) return set_error(SLG_ERR_ARG, "slg_thermo_pack: ldw too large");
+    if (ldw < nw) return set_error(SLG_ERR_ARG, "%s: ldw too small", what);
+    if (!x || !thr || !out) return set_error(SLG_ERR_ARG, "%s: null pointer", what);
+    if (cdiv(ldw, 4) > 65535) return set_error(SLG_ERR_ARG, "%s: ldw too large", what);
     // one CTA row per 4 words up to ldw: words past the batch come out zero
     dim3 grid((unsigned)cdiv(C * HW, TH_FT), (unsigned)cdiv(ldw, 4));
     // mode 2 = mode 0 with thresholds the caller guarantees sorted ascending: binary
@@ -430,15 +462,25 @@ extern "C" int slg_thermo_pack(const float* x, int64_t B, int64_t C, int64_t HW,
         int lg = 0;
         while ((1 << lg) < nt + 1) ++lg;       // 2^lg - 1 >= nt
         switch (lg) {
-            case 1: thermo_kernel<1><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
-            case 2: thermo_kernel<2><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
-            case 3: thermo_kernel<3><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
-            case 4: thermo_kernel<4><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
-            case 5: thermo_kernel<5><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
-            default: thermo_kernel<6><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
+            case 1: thermo_kernel<1, TIn><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
+            case 2: thermo_kernel<2, TIn><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
+            case 3: thermo_kernel<3, TIn><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
+            case 4: thermo_kernel<4, TIn><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
+            case 5: thermo_kernel<5, TIn><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
+            default: thermo_kernel<6, TIn><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, 0, out, ldw, guess); break;
         }
     } else {
-        thermo_kernel<0><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, mode, out, ldw, 0);
+        thermo_kernel<0, TIn><<<grid, 256, 0, st>>>(x, B, C, HW, thr, (int)T, mode, out, ldw, 0);
     }
-    return check_launch("slg_thermo_pack");
+    return check_launch(what);
+}
+
+extern "C" int slg_thermo_pack(const float* x, int64_t B, int64_t C, int64_t HW, const float* thr,
+                               int64_t T, int32_t mode, uint64_t* out, int64_t ldw, void* stream) {
+    return thermo_pack("slg_thermo_pack", x, B, C, HW, thr, T, mode, out, ldw, stream);
+}
+
+extern "C" int slg_thermo_pack_u8(const uint8_t* x, int64_t B, int64_t C, int64_t HW, const float* thr,
+                                  int64_t T, int32_t mode, uint64_t* out, int64_t ldw, void* stream) {
+    return thermo_pack("slg_thermo_pack_u8", x, B, C, HW, thr, T, mode, out, ldw, stream);
 }

@@ -20,11 +20,12 @@ dev = "cuda"
 
 
 def _oracle_counts(cfg, model, enc, x):
-    """Oracle counts for a host batch of the config's raw input."""
+    """Oracle counts for a host batch of the config's raw input (uint8 pixels are the
+    fp32 images k / 255)."""
     sd = {k: v.detach().cpu().numpy() for k, v in model.state_dict().items()}
     spec = net_spec(cfg["ctor"], cfg["kwargs"], sd)
     n = x.shape[0]
-    xn = x.numpy()
+    xn = x.numpy() if cfg["inp"] == "bern" else bench.image_float(x).numpy()
     if cfg["inp"] == "image":
         xn = OH.thermometer_bits(xn, cfg["thresholds"])
     elif cfg["inp"] == "encoder":
@@ -39,7 +40,7 @@ def _bp(cfg, model):
 
 
 def _bp_counts(cfg, bp, enc, x):
-    """Counts through the bit-packed API: uint8 features, or fp32 images with the
+    """Counts through the bit-packed API: uint8 features, or uint8 images with the
     thermometer fused into packing (shared or learned thresholds)."""
     tau = cfg["kwargs"]["tau"]
     if cfg["inp"] == "bern":
@@ -97,7 +98,7 @@ def test_c3_full_batch_vs_oracle():
     m = m.to(dev)
     np.testing.assert_array_equal(_bp_counts(cfg, _bp(cfg, m), None, x), ref)
     import silogic_b200 as S
-    xb = S.binarize_spatial(x.to(dev), cfg["thresholds"])
+    xb = S.binarize_spatial(bench.image_float(x).to(dev), cfg["thresholds"])
     np.testing.assert_array_equal(m.forward_hard(xb).cpu().numpy(), ref)
 
 
@@ -133,7 +134,7 @@ def test_c5_full_net_across_slice_boundaries_vs_oracle(c5):
     B = 2112
     x = bench.make_input(cfg, B, seed=1)
     bp = _bp(cfg, m.to(dev))
-    bp.pipeline_bytes = 1024 * 3 * 32 * 32 * 4          # 1,024-sample slices
+    bp.pipeline_bytes = 1024 * 3 * 32 * 32              # 1,024-sample slices of uint8 pixels
     got = _bp_counts(cfg, bp, None, x)
     mc = m.cpu()
     for lo, hi in ((0, 96), (1000, 1056), (2040, 2112)):
@@ -167,7 +168,9 @@ def _soft_case(key, B):
     if cfg["inp"] == "bern":
         x = x.float()
     elif cfg["inp"] == "image":
-        x = torch.from_numpy(OH.thermometer_bits(x.numpy(), cfg["thresholds"])).float()
+        x = torch.from_numpy(OH.thermometer_bits(bench.image_float(x).numpy(), cfg["thresholds"])).float()
+    else:
+        x = bench.image_float(x)
     return cfg, m, enc, x
 
 

@@ -442,3 +442,57 @@ def test_loaded_packed_artefact_gives_the_same_counts(tmp_path):
     back = load_packed(tmp_path / "net.npz", device=dev)
     x = (np.random.default_rng(0).random((300, 6, 8, 8)) < 0.5).astype(np.uint8)
     np.testing.assert_array_equal(back(x), bp(x))
+
+
+@pytest.mark.parametrize("th", [[0.5], [1 / 6, 2 / 6, 3 / 6, 4 / 6, 5 / 6],
+                                [(i + 1) / 32 for i in range(31)], [0.7, 0.2, 0.5],
+                                [(i + 1) / 40 for i in range(39)],
+                                [k / 255 for k in (0, 1, 2, 127, 128, 254, 255)]])
+@pytest.mark.parametrize("shape", [(70, 3, 5, 7), (1100, 3, 32, 32), (65, 1, 4, 4)])
+def test_thermometer_pack_uint8_equals_float_quotient(th, shape):
+    """uint8 pixels k packed like the fp32 image k / 255 (torchvision ToTensor), for shared
+    sorted / unsorted / long threshold lists, thresholds exactly on k / 255, every pixel
+    value, vector and scalar load paths (3072 and 35 features), and learned per-feature
+    thresholds; checked against the oracle on the float image."""
+    from silogic_b200 import _hard
+    g = torch.Generator().manual_seed(len(th) + shape[0])
+    u8 = torch.randint(0, 256, shape, generator=g, dtype=torch.uint8)
+    u8.view(-1)[:256] = torch.arange(256, dtype=torch.uint8)      # every value appears
+    f32 = u8.float() / 255
+    ref = OH.pack_bits(OH.thermometer_bits(u8.numpy().astype(np.float32) / np.float32(255), th)
+                       .reshape(shape[0], -1))
+    for mode_thr in (th, torch.tensor(th)):                      # sorted-list and tensor paths
+        got = _hard.thermo_pack(u8.to(dev), mode_thr)
+        assert torch.equal(got, _hard.thermo_pack(f32.to(dev), mode_thr))
+        got = got.reshape(-1, got.shape[-1])
+        np.testing.assert_array_equal(got[:, :ref.shape[1]].cpu().numpy().view(np.uint64), ref)
+    F = shape[1] * shape[2] * shape[3]
+    learned = torch.rand(F, len(th), generator=g)
+    assert torch.equal(_hard.thermo_pack(u8.to(dev), learned.to(dev), mode=1),
+                       _hard.thermo_pack(f32.to(dev), learned.to(dev), mode=1))
+
+
+def test_forward_images_uint8_host_batch_equals_float():
+    """BitpackedConvNet.forward_images on a pinned uint8 host batch (pipelined copies)
+    gives the logits of the same images as fp32 k / 255."""
+    import silogic_b200 as S
+    from silogic_b200.bitpacking import convert_logic_conv_net
+    kw = dict(in_channels=15, in_hw=16, channels=[24, 40], head_widths=[160], tree_depth=2,
+              node="gate16", tau=4.0, seed=3)
+    torch.manual_seed(5)
+    m = S.LogicTreeNet(**kw)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.normal_()
+    bp = convert_logic_conv_net(m.cuda())
+    u8 = torch.randint(0, 256, (5000, 3, 16, 16), generator=torch.Generator().manual_seed(6),
+                       dtype=torch.uint8).pin_memory()
+    th = [1 / 6, 2 / 6, 3 / 6, 4 / 6, 5 / 6]
+    old = bp.pipeline_bytes
+    bp.pipeline_bytes = 1 << 20           # several pipelined slices
+    try:
+        got = bp.forward_images(u8, th)
+    finally:
+        bp.pipeline_bytes = old
+    ref = bp.forward_images((u8.float() / 255).cuda(), th)
+    assert torch.equal(got.cpu(), ref.cpu())
