@@ -202,6 +202,10 @@ thermo_kernel(const TIn* __restrict__ x, int64_t B, int64_t C, int64_t HW,
     __shared__ int64_t s_row[TH_FT];       // pixel p of each feature
     __shared__ int32_t s_c[TH_FT];         // channel c of each feature
     __shared__ float s_q[256];             // uint8 input: k / 255
+    // uint8 input with sorted shared thresholds: the tile holds the byte k itself and a
+    // value's count (thresholds <= k / 255) is one lookup in s_cnt
+    constexpr bool U8CNT = sizeof(TIn) == 1 && LOG > 0;
+    __shared__ int32_t s_cnt[U8CNT ? 256 : 1];
     ThermoIn<TIn> cvt;
     if constexpr (sizeof(TIn) == 1) cvt.q = s_q;
     cvt.init();
@@ -237,13 +241,14 @@ thermo_kernel(const TIn* __restrict__ x, int64_t B, int64_t C, int64_t HW,
             const int sr = i / PER, q = (i % PER) * VEC;
             const TIn* e = reinterpret_cast<const TIn*>(&r[k]);
 #pragma unroll
-            for (int j = 0; j < VEC; ++j) tile[sr][q + j] = cvt(e[j]);
+            for (int j = 0; j < VEC; ++j) tile[sr][q + j] = U8CNT ? __int_as_float((int)e[j]) : cvt(e[j]);
         }
     } else {
         for (int i = threadIdx.x; i < TH_S * TH_FT; i += 256) {
             const int sr = i / TH_FT, f = i % TH_FT;
             const int64_t b = b0 + sr, ff = f0 + f;
-            tile[sr][f] = (b < B && ff < F) ? cvt(x[b * F + ff]) : 0.0f;
+            const TIn e = (b < B && ff < F) ? x[b * F + ff] : TIn(0);
+            tile[sr][f] = U8CNT ? __int_as_float((int)e) : cvt(e);
         }
     }
     const int nf = (int)min((int64_t)TH_FT, F - f0);
@@ -268,6 +273,15 @@ thermo_kernel(const TIn* __restrict__ x, int64_t B, int64_t C, int64_t HW,
             }
         }
         __syncthreads();
+        if constexpr (U8CNT) {
+            if (threadIdx.x < 256) {
+                const float v = s_q[threadIdx.x];
+                int cnt = 0;
+                for (int t = 0; t < nt; ++t) cnt += (int)(v >= s_srt[t]);
+                s_cnt[threadIdx.x] = cnt;
+            }
+            __syncthreads();
+        }
         // Sorted shared thresholds that lie within a quarter of their mean spacing of a
         // uniform grid: each value's count (thresholds <= v) is within one of the grid
         // guess floor((v - t_0) / step) + 1, so the guess corrected by two independent
@@ -284,7 +298,7 @@ thermo_kernel(const TIn* __restrict__ x, int64_t B, int64_t C, int64_t HW,
                 ok = fabsf(tv - (u0 + (float)threadIdx.x * step)) <= 0.25f * step &&
                      (threadIdx.x == 0 || s_srt[threadIdx.x - 1] <= tv);
             }
-            uni = __syncthreads_and(ok) != 0;
+            uni = __syncthreads_and(ok) != 0 || U8CNT;
         }
         // Sorted thresholds, one feature per warp item (17-32 thresholds in the chunk):
         // with c_i = count of thresholds <= v_i for the warp's 32 samples, lane t's word
@@ -305,11 +319,16 @@ thermo_kernel(const TIn* __restrict__ x, int64_t B, int64_t C, int64_t HW,
 #pragma unroll
                 for (int h = 0; h < 4; ++h) {
                     const float v = tile[wp * 128 + h * 32 + lane][fa];
-                    // nearest integer of q + 1/2 (exact float rounding, no conversion
-                    // unit): within one of the count, as the comment above requires
-                    const float q = fminf(fmaxf((v - u0) * inv + 0.5f, 0.f), 64.f);
-                    const int gi = min(__float_as_int(q + 12582912.0f) - 0x4B400000, nt);
-                    const int pos = gi + (int)(v >= s_pad[gi + 1]) - (int)(v < s_pad[gi]);
+                    int pos;
+                    if constexpr (U8CNT) {
+                        pos = s_cnt[__float_as_int(v)];
+                    } else {
+                        // nearest integer of q + 1/2 (exact float rounding, no conversion
+                        // unit): within one of the count, as the comment above requires
+                        const float q = fminf(fmaxf((v - u0) * inv + 0.5f, 0.f), 64.f);
+                        const int gi = min(__float_as_int(q + 12582912.0f) - 0x4B400000, nt);
+                        pos = gi + (int)(v >= s_pad[gi + 1]) - (int)(v < s_pad[gi]);
+                    }
                     const uint32_t ok = __ballot_sync(0xffffffffu, b0 + wp * 128 + h * 32 + lane < B);
                     uint32_t gt = 0u;
 #pragma unroll
@@ -349,7 +368,10 @@ thermo_kernel(const TIn* __restrict__ x, int64_t B, int64_t C, int64_t HW,
 #pragma unroll
                 for (int h = 0; h < 4; ++h) {
                     uint32_t m = 0;
-                    if (LOG > 0 && uni) {
+                    if (U8CNT) {
+                        const int pos = s_cnt[__float_as_int(v[h])];
+                        m = ((pos >= 32 ? 0xffffffffu : ((1u << pos) - 1u))) & tmask;
+                    } else if (LOG > 0 && uni) {
                         const float q = (v[h] - u0) * inv;
                         const int g = q >= 0.f ? min((int)fminf(q, 64.f) + 1, nt) : 0;
                         const int pos = g + (int)(v[h] >= s_pad[g + 1]) - (int)(v[h] < s_pad[g]);
