@@ -26,7 +26,8 @@ Timing: CUDA events on the launching stream around each step, L2 flushed (a
 256 MB write read back, untimed) before each step, W >= 3 warm-up steps, barrier +
 synchronize around the timed loop, max over ranks.  "e2e" runs the same work
 through the public API from pinned host memory with the host<->device copies
-inside the timed region.  "parity" compares (untimed) the timed step's counts of
+inside the timed region; image configs send uint8 pixels (pixel k = fp32 k/255, as
+torchvision's ToTensor gives), and "e2e_f32" sends the same images as fp32.  "parity" compares (untimed) the timed step's counts of
 the first 128 samples with the CPU oracle; "cpu_baseline" times the reference's
 own CPU path (baseline/_ref) on a bounded sample of the same batch and says
 whether its counts equal the GPU's.
@@ -360,11 +361,14 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
                                                      counts_all.to(wdt).view(torch.uint8))
         return counts_all
 
-    def step_e2e():
+    # the same images as fp32 k / 255 on the host, for the fp32-input end-to-end figure
+    x_host_f32 = image_float(x_host).pin_memory() if cfg["inp"] != "bern" else None
+
+    def step_e2e(src=x_host):
         outs = []
         for c in range(nchunks):
             n = min(chunk, B - c * chunk)
-            xd = x_host[:n]     # pinned host batch: copied into the graph's static input
+            xd = src[:n]        # pinned host batch: copied into the graph's static input
             if cfg["inp"] == "bern":
                 outs.append(bp.forward(xd).to("cpu", non_blocking=True))
             else:
@@ -409,6 +413,21 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
             e1.synchronize()
             e2e_times.append(e0.elapsed_time(e1))
         e2e_ms = statistics.mean(e2e_times)
+        e2e_f32_ms = 0.0
+        if x_host_f32 is not None:
+            step_e2e(x_host_f32)
+            torch.cuda.synchronize()
+            e2e_times = []
+            for _ in range(steps):
+                flush_l2(flush)
+                e0, e1 = events()
+                e0.record()
+                step_e2e(x_host_f32)
+                e1.record()
+                e1.synchronize()
+                e2e_times.append(e0.elapsed_time(e1))
+            e2e_f32_ms = statistics.mean(e2e_times)
+            del x_host_f32
     if ws > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
@@ -429,7 +448,7 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
     in_bytes = x_host[:1].numel() * x_host.element_size()
     step_device(collective=False)
     torch.cuda.synchronize()
-    return dict(ms=ms, e2e_ms=e2e_ms, kern=kern, per_kind=per_kind, x_first=x_host,
+    return dict(ms=ms, e2e_ms=e2e_ms, e2e_f32_ms=e2e_f32_ms, kern=kern, per_kind=per_kind, x_first=x_host,
                 counts_first=counts_all[:chunk].cpu(), enc=enc, model=model,
                 bytes_per_sample=sum(b for _, b in stage), launches_per_step=launches[0] / steps,
                 clocks=clk.summary(), h2d=int(in_bytes * B), d2h=int(B * plan.num_classes * 4))
@@ -754,10 +773,11 @@ def measure_ours(cfg_key, cfg, a, ws, rank, dev, warmup, with_soft=True, check=T
     soft = None
     if with_soft and cfg["soft_batch"]:
         soft = run_soft(cfg, cfg["soft_batch"], a.steps, warmup, rank, ws, dev)
-    ms = torch.tensor([r["ms"], r["e2e_ms"], soft["ms"] if soft else 0.0], device=dev)
+    ms = torch.tensor([r["ms"], r["e2e_ms"], soft["ms"] if soft else 0.0, r["e2e_f32_ms"]],
+                      device=dev)
     if ws > 1:
         torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
-    ms_step, e2e_ms, soft_ms = ms.tolist()
+    ms_step, e2e_ms, soft_ms, e2e_f32_ms = ms.tolist()
     hbm, kind = peaks()
     dom = max(r["kern"], key=lambda k: r["kern"][k][0])
     dom_ms, dom_n = r["kern"][dom]
@@ -768,6 +788,10 @@ def measure_ours(cfg_key, cfg, a, ws, rank, dev, warmup, with_soft=True, check=T
         "value": total / (ms_step * 1e-3), "ms_per_step": ms_step, "B": B, "total": total,
         "e2e": {"value": total / (e2e_ms * 1e-3), "unit": "samples/s",
                 "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+        "e2e_f32": ({"value": total / (e2e_f32_ms * 1e-3), "unit": "samples/s",
+                     "h2d_bytes_per_step": r["h2d"] * 4, "d2h_bytes_per_step": r["d2h"],
+                     "input": "the same images as fp32 k/255 from pinned host memory"}
+                    if e2e_f32_ms > 0 else None),
         "gpu_launches": int(round(r["launches_per_step"] * a.steps)),
         "roofline": {"kernel": f"slg_{dom} ({dom_n:.0f} launches/step)", "bound": "hbm",
                      "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
@@ -903,7 +927,7 @@ def main():
                        "l2": "flushed before each step (256 MB write, then read back so L2 is clean)",
                        "launch": "one CUDA graph per chunk shape (pack + every layer + GroupSum)",
                        "clocks": "sampled over >= 1 s of untimed replays of the same step, then the timed steps"},
-            "e2e": res["e2e"], "gpu_launches": res["gpu_launches"], "roofline": res["roofline"],
+            "e2e": res["e2e"], "e2e_f32": res.get("e2e_f32"), "gpu_launches": res["gpu_launches"], "roofline": res["roofline"],
             "kernels_ms_per_step": res["kernels_ms_per_step"], "clocks": res["clocks"],
             "parity": res.get("parity"),
         }
