@@ -235,12 +235,17 @@ class BitpackedNet:
         return logits
 
     #: host batches are pipelined (see _run_pipelined) in slices of about this many
-    #: input bytes (a multiple of 1024 samples), when there are at least two slices
+    #: input bytes (a multiple of 1024 samples), when there are at least two slices ...
     pipeline_bytes = 8 << 20
+    #: ... and of at least this many samples, so that each replay still fills the GPU
+    #: (C5 from uint8 pixels: 3,072-sample slices ran at 8.3 M samples/s end to end,
+    #: 16,384-sample ones at 11.1 M, 65,536-sample ones at 8.7 M)
+    min_slice_samples = 16384
 
     def _slice(self, t):
         per = max(1, t[:1].numel() * t.element_size())
-        return max(1024, -(-(self.pipeline_bytes // per) // 1024) * 1024)
+        by_bytes = -(-(self.pipeline_bytes // per) // 1024) * 1024
+        return max(1024, self.min_slice_samples, by_bytes)
 
     def _run(self, x, thresholds=None, mode=0):
         """Logits of a numpy / host / device batch; host tensors are copied straight

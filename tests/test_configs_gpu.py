@@ -135,6 +135,7 @@ def test_c5_full_net_across_slice_boundaries_vs_oracle(c5):
     x = bench.make_input(cfg, B, seed=1)
     bp = _bp(cfg, m.to(dev))
     bp.pipeline_bytes = 1024 * 3 * 32 * 32              # 1,024-sample slices of uint8 pixels
+    bp.min_slice_samples = 1024
     got = _bp_counts(cfg, bp, None, x)
     mc = m.cpu()
     for lo, hi in ((0, 96), (1000, 1056), (2040, 2112)):

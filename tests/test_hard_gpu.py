@@ -303,6 +303,7 @@ def test_pipelined_host_batches_match_one_shot():
     x = (torch.rand(5000, 100, generator=torch.Generator().manual_seed(9)) < 0.3).to(torch.uint8)
     ref = bp(x.cuda()).cpu().numpy()
     bp.pipeline_bytes = 100 * 1024            # 1024-sample slices of 100 features
+    bp.min_slice_samples = 1024
     for xin in (x.pin_memory(), x, x.numpy()):
         got = bp(xin)
         got = got if isinstance(got, np.ndarray) else got.cpu().numpy()
@@ -490,6 +491,7 @@ def test_forward_images_uint8_host_batch_equals_float():
     th = [1 / 6, 2 / 6, 3 / 6, 4 / 6, 5 / 6]
     old = bp.pipeline_bytes
     bp.pipeline_bytes = 1 << 20           # several pipelined slices
+    bp.min_slice_samples = 1024
     try:
         got = bp.forward_images(u8, th)
     finally:

@@ -157,3 +157,20 @@ def test_packed_artefact_round_trip_and_corrupt_wiring(tmp_path):
     np.savez(tmp_path / "other.npz", **z)
     with pytest.raises(ValueError):
         load_packed(tmp_path / "other.npz", device="cpu")
+
+
+def test_pipeline_slice_size_rule():
+    """Host batches are sliced by bytes (multiples of 1024 samples) with a floor of
+    min_slice_samples, so per-slice replays of heavy networks still fill the GPU."""
+    from types import SimpleNamespace
+    from silogic_b200.bitpacking.packed import BitpackedConvNet
+    ns = SimpleNamespace(pipeline_bytes=8 << 20, min_slice_samples=16384)
+    img_u8 = torch.zeros(4, 3, 32, 32, dtype=torch.uint8)     # 3,072 B per sample
+    feats = torch.zeros(4, 784, dtype=torch.uint8)             # 784 B per sample
+    assert BitpackedConvNet._slice(ns, img_u8) == 16384
+    assert BitpackedConvNet._slice(ns, img_u8.float()) == 16384
+    ns.min_slice_samples = 1024
+    assert BitpackedConvNet._slice(ns, img_u8) == 3072
+    assert BitpackedConvNet._slice(ns, feats) == 11264
+    ns.pipeline_bytes = 1
+    assert BitpackedConvNet._slice(ns, feats) == 1024
