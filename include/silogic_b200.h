@@ -94,7 +94,7 @@ int slg_check_index_range(const int32_t* idx, int64_t count, int64_t limit, void
 /* Process-wide tuning knobs (thread-safe; the defaults are the measured best):
  *   key 0  arity-2 conv trees use the uniform gate-dispatch kernel (1) or the
  *          generic LUT-tree kernel (0); both give identical bits;
- *   key 1  pooled positions per thread in that kernel (16);
+ *   key 1  pooled positions per thread in that kernel (32);
  *   key 2  sorted near-uniform thermometer thresholds use the grid guess with two
  *          corrective comparisons (1) or a binary search (0); both give identical bits;
  *   key 3  node form in the gate-dispatch kernel: one branch on the gate code per node

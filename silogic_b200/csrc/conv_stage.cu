@@ -27,7 +27,7 @@ constexpr int ST_TY = ST_TPH * 2 + 2, ST_TX = ST_TPW * 2 + 2;   // pixel window 
 constexpr int ST_QY = ST_TY / 2, ST_QX = ST_TX / 2;     // per parity phase
 constexpr int ST_PLANE = ST_TY * ST_TX;                 // 16-byte vectors per plane
 
-constexpr int64_t G2_OUTPUTS_PER_CTA = 256 * 16;  // per-channel kernel: threads x positions
+constexpr int64_t G2_OUTPUTS_PER_CTA = 256 * 32;  // per-channel kernel: threads x positions
 constexpr int ST_SMEM_MAX = 227 * 1024;              // opt-in shared memory per CTA
 
 int conv_stage_max_planes() { return ST_SMEM_MAX / (ST_PLANE * 16); }
@@ -261,7 +261,7 @@ bool launch_conv_stage(const uint4* x, int64_t cin, int H, int W, int nvec, cons
     // pipe wavefronts per output), so it only wins where the per-channel kernel cannot
     // fill the GPU: measured 1.35x faster on 128 channels x 16x16 pooled x 4,096 samples
     // (1 M outputs), 1.35x slower on 1024 x 16x16 x 131,072.  Cut-over: the per-channel
-    // kernel's outputs (16 pooled positions per thread, 256 threads per CTA) fill fewer
+    // kernel's outputs (32 pooled positions per thread, 256 threads per CTA) fill fewer
     // than two waves of 2 CTAs per SM.
     const int64_t outputs = n_out * (int64_t)Hp * Wp * nvec;
     if (tuning(T_CONV_STAGE) == 1 && outputs >= 2ll * 2 * sm_count() * G2_OUTPUTS_PER_CTA) return false;

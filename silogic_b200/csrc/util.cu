@@ -40,7 +40,7 @@ int sm_count() {
     return cache[dev];
 }
 
-static std::atomic<int64_t> g_tuning[T_NUM_KEYS] = {{1}, {16}, {1}, {0}, {1}};
+static std::atomic<int64_t> g_tuning[T_NUM_KEYS] = {{1}, {32}, {1}, {0}, {1}};
 
 int64_t tuning(int key) { return (key >= 0 && key < T_NUM_KEYS) ? g_tuning[key].load() : 0; }
 

@@ -137,7 +137,7 @@ def test_tuning_keys_and_env():
     import sys
     L = _lib.lib()
     ranges = {0: (0, 1), 1: (1, 64), 2: (0, 1), 3: (0, 2), 4: (0, 2)}
-    defaults = {0: 1, 1: 16, 2: 1, 3: 0, 4: 1}
+    defaults = {0: 1, 1: 32, 2: 1, 3: 0, 4: 1}
     try:
         for key, (lo, hi) in ranges.items():
             assert L.slg_tuning_set(key, lo) == 0 and L.slg_tuning_set(key, hi) == 0
