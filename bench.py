@@ -362,7 +362,8 @@ def run_hard(cfg, B, steps, warmup, rank, ws, dev):
         return counts_all
 
     # the same images as fp32 k / 255 on the host, for the fp32-input end-to-end figure
-    x_host_f32 = image_float(x_host).pin_memory() if cfg["inp"] != "bern" else None
+    # (one GPU only: 4x the pinned host memory of the uint8 batch per rank)
+    x_host_f32 = image_float(x_host).pin_memory() if cfg["inp"] != "bern" and ws == 1 else None
 
     def step_e2e(src=x_host):
         outs = []
