@@ -406,8 +406,12 @@ thermo_kernel(const TIn* __restrict__ x, int64_t B, int64_t C, int64_t HW,
                 uint64_t* dst = out + (ch * HW + s_row[f]) * ldw + w;
                 const uint64_t lo = ((uint64_t)wd[1] << 32) | wd[0];
                 const uint64_t hi = ((uint64_t)wd[3] << 32) | wd[2];
-                if (w + 2 <= ldw) *reinterpret_cast<uint4*>(dst) = make_uint4((uint32_t)lo, (uint32_t)(lo >> 32), (uint32_t)hi, (uint32_t)(hi >> 32));
-                else if (w < ldw) dst[0] = lo;
+                // 16-byte stores only when every row starts on a 16-byte boundary (even ldw)
+                if ((ldw & 1) == 0 && w + 2 <= ldw) *reinterpret_cast<uint4*>(dst) = make_uint4((uint32_t)lo, (uint32_t)(lo >> 32), (uint32_t)hi, (uint32_t)(hi >> 32));
+                else {
+                    if (w < ldw) dst[0] = lo;
+                    if (w + 1 < ldw) dst[1] = hi;
+                }
             }
         }
     }

@@ -498,3 +498,24 @@ def test_forward_images_uint8_host_batch_equals_float():
         bp.pipeline_bytes = old
     ref = bp.forward_images((u8.float() / 255).cuda(), th)
     assert torch.equal(got.cpu(), ref.cpu())
+
+
+
+@pytest.mark.parametrize("B, ldw", [(1000, None), (777, 13), (4160, 70), (300, 9), (64, 1)])
+@pytest.mark.parametrize("T", [1, 5, 31, 39])
+def test_thermometer_pack_any_row_length_vs_oracle(B, ldw, T):
+    """Caller-chosen row lengths: odd ldw (rows not 16-byte aligned, so 8-byte stores),
+    rows padded past the batch (zero words) and a ragged batch, for sorted threshold
+    lists of one, a few, 31 and more than one 32-threshold chunk."""
+    from silogic_b200 import _hard
+    g = torch.Generator().manual_seed(B + T)
+    u8 = torch.randint(0, 256, (B, 3, 8, 16), generator=g, dtype=torch.uint8)
+    u8.view(-1)[:256] = torch.arange(256, dtype=torch.uint8)
+    th = sorted(torch.rand(T, generator=g).tolist())
+    got = _hard.thermo_pack(u8.to(dev), th, ldw=ldw)
+    ref = OH.pack_bits(OH.thermometer_bits(u8.numpy().astype(np.float32) / np.float32(255), th)
+                       .reshape(B, -1))
+    w = got.reshape(-1, got.shape[-1]).cpu().numpy().view(np.uint64)
+    assert w.shape[1] >= ref.shape[1]
+    np.testing.assert_array_equal(w[:, :ref.shape[1]], ref)
+    assert not w[:, ref.shape[1]:].any()
