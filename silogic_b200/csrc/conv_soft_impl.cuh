@@ -412,6 +412,22 @@ conv_soft_bwd_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict
     }
 }
 
+// Sum workspace rows in place, in a fixed order (deterministic): rows k = 0..nrows-1 sit
+// at memory rows k * rstride; thread (column i, group g) adds rows [g*rpg, (g+1)*rpg) in
+// ascending order and writes the sum over the group's first row.  Each thread reads and
+// writes only its own column of its own group, so nothing races.  Two launches reduce
+// every (channel, part) column to row 0: groups of CS_ROWGRP rows, then the group sums.
+constexpr int CS_ROWGRP = 32;
+static __global__ void conv_soft_rowsum_kernel(float* __restrict__ ws, int64_t width, int64_t rstride,
+                                               int64_t nrows, int64_t rpg) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= width) return;
+    const int64_t k0 = (int64_t)blockIdx.y * rpg, k1 = min(nrows, k0 + rpg);
+    float t = 0.f;
+    for (int64_t k = k0; k < k1; ++k) t += ws[k * rstride * width + i];
+    ws[k0 * rstride * width + i] = t;
+}
+
 // one thread per output channel: sum the workspace rows and apply the Jacobians
 template <int NODE, int AR, int D>
 __global__ void conv_soft_finish_kernel(const float* __restrict__ ws, int64_t rows, ConvArgs A,
@@ -490,7 +506,17 @@ inline void conv_launch_bwd(const ConvArgs& A, const float* gy, float* gx, float
     dim3 grid((unsigned)(A.n_out * conv_tiles(A)), (unsigned)conv_chunks(A));
     conv_soft_bwd_kernel<NODE, AR, D, KT><<<grid, CS_WARPS * 32, 0, st>>>(A, gy, gx, ws, npart);
     const int64_t rows = conv_chunks(A) * conv_tiles(A);
-    conv_soft_finish_kernel<NODE, AR, D><<<(unsigned)cdiv(A.n_out, 64), 64, 0, st>>>(ws, rows, A, npart,
+    const int64_t width = A.n_out * npart;
+    if (rows > 1) {
+        const int64_t rpg = std::max<int64_t>(CS_ROWGRP, cdiv(rows, 65535));
+        const int64_t groups = cdiv(rows, rpg);
+        conv_soft_rowsum_kernel<<<dim3((unsigned)cdiv(width, 256), (unsigned)groups), 256, 0, st>>>(
+            ws, width, 1, rows, rpg);
+        if (groups > 1)
+            conv_soft_rowsum_kernel<<<dim3((unsigned)cdiv(width, 256), 1), 256, 0, st>>>(
+                ws, width, rpg, groups, groups);
+    }
+    conv_soft_finish_kernel<NODE, AR, D><<<(unsigned)cdiv(A.n_out, 64), 64, 0, st>>>(ws, 1, A, npart,
                                                                                       gconn, gparams);
 }
 
