@@ -103,7 +103,10 @@ int slg_check_index_range(const int32_t* idx, int64_t count, int64_t limit, void
  *   key 4  arity-2 3x3 2x2-pooled blocks whose input planes fit one shared-memory
  *          window with per-channel tables (227 KB: about 130 planes) can stage it and
  *          evaluate every output channel from it: when the per-channel kernel would not
- *          fill two waves (1), always (2), never (0); identical bits.
+ *          fill two waves (1), always (2), never (0); identical bits;
+ *   key 5  soft backward of one-level arity-6 multilinear conv trees (64-entry LUTs,
+ *          no wire residual): the low-register factorised kernel (1) or the generic
+ *          tree kernel (0); the same gradients up to fp32 summation order.
  * No counterpart in the reference (its Triton kernels take fixed block sizes). */
 int slg_tuning_set(int32_t key, int64_t value);
 

@@ -22,7 +22,7 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 int sm_count();
 
 // Process-wide tuning knobs (slg_tuning_set); defaults are the measured best.
-enum TuningKey { T_CONV_GATE2 = 0, T_CONV_PPT = 1, T_THERMO_GUESS = 2, T_CONV_NODE = 3, T_CONV_STAGE = 4, T_NUM_KEYS = 5 };
+enum TuningKey { T_CONV_GATE2 = 0, T_CONV_PPT = 1, T_THERMO_GUESS = 2, T_CONV_NODE = 3, T_CONV_STAGE = 4, T_CONV_ML6 = 5, T_NUM_KEYS = 6 };
 int64_t tuning(int key);
 
 // Arity-2 conv tree blocks with uniform gate dispatch (conv_gate2.cu); false when the

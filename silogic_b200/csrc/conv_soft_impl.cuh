@@ -412,6 +412,224 @@ conv_soft_bwd_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict
     }
 }
 
+// Backward of one-level arity-6 multilinear trees (64-entry LUTs): the form above keeps
+// 64 LUT-gradient and L*K connection-gradient accumulators per thread across its samples
+// and spills.  Here each thread keeps four.
+//  * Node math: split the LUT index q = lo + 8*hi (lo: inputs 0-2, hi: inputs 3-5), so
+//    the weight of entry q is u[lo] * v[hi] with u, v the 8 products of (a_j or 1 - a_j)
+//    over each half.  One pass over the 64 entries gives T[hi] = sum_lo LUT u[lo] and
+//    S[lo] = sum_hi LUT v[hi]; the input derivatives are then differences of S (inputs
+//    0-2) or T (inputs 3-5) weighted by the pair products of the other two inputs.
+//  * Reductions: each round (one sample per lane) every lane writes its sample's u,
+//    g*v, tap values and leaf adjoints into its warp's buffer (row-major, one column per
+//    sample), and lane l then sums, over the 32 samples, LUT entries l and l + 32 (u*gv)
+//    and connection entries l and l + 32 (tap * leaf adjoint) with 16-byte loads.
+// Same workspace rows as conv_soft_bwd_kernel.  Dynamic shared memory: ml6_smem_bytes().
+constexpr int ML6_ROW = 36;                       // floats per buffer row (32 samples + pad)
+template <int KT>
+__host__ __device__ constexpr int ml6_rows() { return 8 + 8 + 6 * KT + 6; }     // u, g*v, taps, leaf adjoints
+template <int KT>
+constexpr int ml6_smem_bytes() { return CS_WARPS * ml6_rows<KT>() * ML6_ROW * 4; }
+
+template <int KT>
+__global__ void __launch_bounds__(CS_WARPS * 32, 2)
+conv_soft_bwd_ml6_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict__ gx,
+                         float* __restrict__ ws, int npart) {
+    constexpr int L = 6, NPG = 64;
+    __shared__ ConvSmem<N_MULTI, 6, 1> S;
+    __shared__ float red[CS_WARPS][L * KT + NPG];
+    __shared__ int s_pos[CS_WARPS][4 * L * KT];
+    extern __shared__ __align__(16) float ml6_buf[];
+    const int npos = A.Hp * A.Wp;
+    const int tiles = (npos + CS_WARPS - 1) / CS_WARPS;
+    const int64_t n = blockIdx.x / tiles;
+    const int tile = blockIdx.x % tiles;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int p = tile * CS_WARPS + warp;
+    float* wrow = ws + (((int64_t)blockIdx.y * tiles + tile) * A.n_out + n) * npart;
+    conv_stage<N_MULTI, 6, 1>(S, A, n);
+    int* pos = s_pos[warp];
+    if (p < npos) conv_fill_pos<N_MULTI, 6, 1, KT>(S, A, p / A.Wp, p % A.Wp, pos, lane);
+    float* buf = ml6_buf + warp * ml6_rows<KT>() * ML6_ROW;
+    float* bu = buf;                               // [8][ML6_ROW]   u
+    float* bh = buf + 8 * ML6_ROW;                 // [8][ML6_ROW]   g * v
+    float* bx = buf + 16 * ML6_ROW;                // [L*KT][ML6_ROW] tap values
+    float* bg = buf + (16 + L * KT) * ML6_ROW;     // [L][ML6_ROW]   leaf adjoints
+    const int K = A.K;
+    const float* lut = S.np;                       // 64 staged LUT values (sigmoid of the raw)
+    float accL0 = 0.f, accL1 = 0.f, accC0 = 0.f, accC1 = 0.f;
+    // this lane's entries: LUT q = lane, lane + 32 (lo = lane & 7, hi = lane >> 3, + 4);
+    // connection e = lane, lane + 32 (rows (e / K) * KT + e % K of bx, row e / K of bg)
+    const int qlo = lane & 7, qhi = lane >> 3;
+    const int e0 = lane, e1 = lane + 32;
+    const bool has0 = e0 < L * K, has1 = e1 < L * K;
+    const int xr0 = has0 ? (e0 / K) * KT + e0 % K : 0, xr1 = has1 ? (e1 / K) * KT + e1 % K : 0;
+    const int gr0 = has0 ? e0 / K : 0, gr1 = has1 ? e1 / K : 0;
+
+    if (p < npos) {
+        const int64_t b0 = (int64_t)blockIdx.y * (32 * CS_ITER);
+        float vals[2 * L];
+        for (int it = 0; it < CS_ITER; ++it) {
+            if (b0 + it * 32 >= A.ldb) break;              // warp-uniform
+            // lanes past the batch stay in the loop (the warp shares the buffer) and
+            // contribute zeros
+            const bool live = b0 + it * 32 + lane < A.ldb;
+            const int64_t b = live ? b0 + it * 32 + lane : b0;
+            const float g = live ? gy[((n * npos) + p) * A.ldb + b] : 0.f;
+            int bq = 0;
+            if (A.pool > 1 && A.pool_arg) {
+                bq = A.pool_arg[((n * npos) + p) * A.ldb + b];
+            } else if (A.pool > 1) {
+                float best = 0.f;
+                for (int q = 0; q < A.pool * A.pool; ++q) {
+                    const float v = conv_tree_value<N_MULTI, 6, 1, KT>(S, A, pos + q * L * KT, b, vals);
+                    if (q == 0 || v > best) { best = v; bq = q; }
+                }
+            }
+            const int* posq = pos + bq * L * KT;
+            // leaf values; tap values go to the buffer for the connection gradients
+            // one leaf at a time (KT loads in flight, not L*KT); each leaf value is shifted
+            // in at the top so the array keeps fixed register indices
+            float a[L];
+#pragma unroll 1
+            for (int l = 0; l < L; ++l) {
+                float sl = 0.f;
+#pragma unroll
+                for (int k = 0; k < KT; ++k) {
+                    float v = 0.f;
+                    if (k < K) {
+                        const int pp = posq[l * K + k];
+                        if (pp >= 0 && live) v = __ldg(&A.x[(int64_t)pp * A.ldb + b]);
+                        sl += S.w[l * K + k] * v;
+                    }
+                    bx[(l * KT + k) * ML6_ROW + lane] = v;
+                }
+#pragma unroll
+                for (int i = 0; i < L - 1; ++i) a[i] = a[i + 1];
+                a[L - 1] = sl;
+            }
+            // half products and pair products of each half
+            float u[8], v[8];
+            {
+                const float f0[2] = {1.f - a[0], a[0]}, f1[2] = {1.f - a[1], a[1]}, f2[2] = {1.f - a[2], a[2]};
+                const float h0[2] = {1.f - a[3], a[3]}, h1[2] = {1.f - a[4], a[4]}, h2[2] = {1.f - a[5], a[5]};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    u[i] = f0[i & 1] * f1[(i >> 1) & 1] * f2[i >> 2];
+                    v[i] = h0[i & 1] * h1[(i >> 1) & 1] * h2[i >> 2];
+                }
+            }
+            float T[8], Sx[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { T[i] = 0.f; Sx[i] = 0.f; }
+#pragma unroll
+            for (int hi = 0; hi < 8; ++hi) {
+#pragma unroll
+                for (int l4 = 0; l4 < 2; ++l4) {
+                    const float4 t4 = *reinterpret_cast<const float4*>(lut + hi * 8 + l4 * 4);
+                    const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const int lo = l4 * 4 + c;
+                        T[hi] += tv[c] * u[lo];
+                        Sx[lo] += tv[c] * v[hi];
+                    }
+                }
+            }
+            // dy/da_j: sum over the other two bits of the half of (pair product) x
+            // (S or T at bit j = 1 minus bit j = 0)
+            float da[L];
+#pragma unroll
+            for (int j = 0; j < 3; ++j) {
+                float dl = 0.f, dh = 0.f;
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    // r enumerates the other two bits (low one first)
+                    const int o1 = r & 1, o2 = r >> 1;
+                    int i0, i1;
+                    float pl, ph;
+                    if (j == 0) {
+                        i0 = (o1 << 1) | (o2 << 2);
+                        pl = (o1 ? a[1] : 1.f - a[1]) * (o2 ? a[2] : 1.f - a[2]);
+                        ph = (o1 ? a[4] : 1.f - a[4]) * (o2 ? a[5] : 1.f - a[5]);
+                    } else if (j == 1) {
+                        i0 = o1 | (o2 << 2);
+                        pl = (o1 ? a[0] : 1.f - a[0]) * (o2 ? a[2] : 1.f - a[2]);
+                        ph = (o1 ? a[3] : 1.f - a[3]) * (o2 ? a[5] : 1.f - a[5]);
+                    } else {
+                        i0 = o1 | (o2 << 1);
+                        pl = (o1 ? a[0] : 1.f - a[0]) * (o2 ? a[1] : 1.f - a[1]);
+                        ph = (o1 ? a[3] : 1.f - a[3]) * (o2 ? a[4] : 1.f - a[4]);
+                    }
+                    i1 = i0 | (1 << j);
+                    dl += pl * (Sx[i1] - Sx[i0]);
+                    dh += ph * (T[i1] - T[i0]);
+                }
+                da[j] = dl;
+                da[3 + j] = dh;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                bu[i * ML6_ROW + lane] = u[i];
+                bh[i * ML6_ROW + lane] = g * v[i];
+            }
+            // leaves -> taps: dL/dx through the connection weights
+#pragma unroll
+            for (int l = 0; l < L; ++l) bg[l * ML6_ROW + lane] = g * da[l];
+#pragma unroll 1
+            for (int l = 0; l < L; ++l) {
+                const float gl = bg[l * ML6_ROW + lane];
+#pragma unroll
+                for (int k = 0; k < KT; ++k) {
+                    if (k < K) {
+                        const int e = l * K + k;
+                        const int pp = posq[e];
+                        if (pp >= 0 && live) {
+                            const int64_t idx = (int64_t)pp * A.ldb + b;
+                            if (A.gleaf)
+                                A.gleaf[((n * (L * K) + e) * (int64_t)npos + p) * A.ldb + b] = gl * S.w[e];
+                            else if (gx && S.w[e] != 0.0f) atomicAdd(&gx[idx], gl * S.w[e]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            // this lane's entries, summed over the round's 32 samples
+#pragma unroll
+            for (int s4 = 0; s4 < 32; s4 += 4) {
+                const float4 uu = *reinterpret_cast<const float4*>(bu + qlo * ML6_ROW + s4);
+                const float4 h0 = *reinterpret_cast<const float4*>(bh + qhi * ML6_ROW + s4);
+                const float4 h1 = *reinterpret_cast<const float4*>(bh + (qhi + 4) * ML6_ROW + s4);
+                accL0 += uu.x * h0.x + uu.y * h0.y + uu.z * h0.z + uu.w * h0.w;
+                accL1 += uu.x * h1.x + uu.y * h1.y + uu.z * h1.z + uu.w * h1.w;
+                if (has0) {
+                    const float4 xv = *reinterpret_cast<const float4*>(bx + xr0 * ML6_ROW + s4);
+                    const float4 gv = *reinterpret_cast<const float4*>(bg + gr0 * ML6_ROW + s4);
+                    accC0 += xv.x * gv.x + xv.y * gv.y + xv.z * gv.z + xv.w * gv.w;
+                }
+                if (has1) {
+                    const float4 xv = *reinterpret_cast<const float4*>(bx + xr1 * ML6_ROW + s4);
+                    const float4 gv = *reinterpret_cast<const float4*>(bg + gr1 * ML6_ROW + s4);
+                    accC1 += xv.x * gv.x + xv.y * gv.y + xv.z * gv.z + xv.w * gv.w;
+                }
+            }
+            __syncwarp();
+        }
+    }
+    // per-warp partials (every lane owns distinct entries), then across the CTA's warps
+    red[warp][L * KT + lane] = accL0;
+    red[warp][L * KT + lane + 32] = accL1;
+    if (has0) red[warp][xr0] = accC0;
+    if (has1) red[warp][xr1] = accC1;
+    __syncthreads();
+    for (int e = threadIdx.x; e < L * K + NPG; e += blockDim.x) {
+        const int src = e < L * K ? (e / K) * KT + (e % K) : L * KT + (e - L * K);
+        float t = 0.f;
+        for (int w = 0; w < CS_WARPS; ++w) t += red[w][src];
+        wrow[e] = t;
+    }
+}
+
 // Sum workspace rows in place, in a fixed order (deterministic): rows k = 0..nrows-1 sit
 // at memory rows k * rstride; thread (column i, group g) adds rows [g*rpg, (g+1)*rpg) in
 // ascending order and writes the sum over the group's first row.  Each thread reads and
@@ -504,7 +722,17 @@ inline void conv_launch_bwd(const ConvArgs& A, const float* gy, float* gx, float
     constexpr int NODES = TreeShape<AR, D>::NODES;
     const int npart = L * A.K + NODES * NodeSize<NODE, AR>::NPG;
     dim3 grid((unsigned)(A.n_out * conv_tiles(A)), (unsigned)conv_chunks(A));
-    conv_soft_bwd_kernel<NODE, AR, D, KT><<<grid, CS_WARPS * 32, 0, st>>>(A, gy, gx, ws, npart);
+    bool done = false;
+    if constexpr (NODE == N_MULTI && AR == 6 && D == 1 && KT <= 8) {
+        // one-level 64-entry LUT trees (no wire residual): the low-register backward
+        if (A.wire_r == 0 && tuning(T_CONV_ML6) == 1 &&
+            cudaFuncSetAttribute(conv_soft_bwd_ml6_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 ml6_smem_bytes<KT>()) == cudaSuccess) {
+            conv_soft_bwd_ml6_kernel<KT><<<grid, CS_WARPS * 32, ml6_smem_bytes<KT>(), st>>>(A, gy, gx, ws, npart);
+            done = true;
+        }
+    }
+    if (!done) conv_soft_bwd_kernel<NODE, AR, D, KT><<<grid, CS_WARPS * 32, 0, st>>>(A, gy, gx, ws, npart);
     const int64_t rows = conv_chunks(A) * conv_tiles(A);
     const int64_t width = A.n_out * npart;
     if (rows > 1) {

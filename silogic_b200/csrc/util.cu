@@ -40,7 +40,7 @@ int sm_count() {
     return cache[dev];
 }
 
-static std::atomic<int64_t> g_tuning[T_NUM_KEYS] = {{1}, {32}, {1}, {0}, {1}};
+static std::atomic<int64_t> g_tuning[T_NUM_KEYS] = {{1}, {32}, {1}, {0}, {1}, {1}};
 
 int64_t tuning(int key) { return (key >= 0 && key < T_NUM_KEYS) ? g_tuning[key].load() : 0; }
 
@@ -50,7 +50,7 @@ extern "C" int slg_tuning_set(int32_t key, int64_t value) {
     using namespace slg;
     if (key < 0 || key >= T_NUM_KEYS) return set_error(SLG_ERR_ARG, "slg_tuning_set: unknown key %d", key);
     if ((key == T_CONV_PPT && (value < 1 || value > 64)) ||
-        ((key == T_CONV_GATE2 || key == T_THERMO_GUESS) && value != 0 && value != 1) ||
+        ((key == T_CONV_GATE2 || key == T_THERMO_GUESS || key == T_CONV_ML6) && value != 0 && value != 1) ||
         (key == T_CONV_STAGE && (value < 0 || value > 2)) ||
         (key == T_CONV_NODE && (value < 0 || value > 2)))
         return set_error(SLG_ERR_ARG, "slg_tuning_set: value %lld out of range for key %d",

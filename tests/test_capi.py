@@ -136,13 +136,13 @@ def test_tuning_keys_and_env():
     import subprocess
     import sys
     L = _lib.lib()
-    ranges = {0: (0, 1), 1: (1, 64), 2: (0, 1), 3: (0, 2), 4: (0, 2)}
-    defaults = {0: 1, 1: 32, 2: 1, 3: 0, 4: 1}
+    ranges = {0: (0, 1), 1: (1, 64), 2: (0, 1), 3: (0, 2), 4: (0, 2), 5: (0, 1)}
+    defaults = {0: 1, 1: 32, 2: 1, 3: 0, 4: 1, 5: 1}
     try:
         for key, (lo, hi) in ranges.items():
             assert L.slg_tuning_set(key, lo) == 0 and L.slg_tuning_set(key, hi) == 0
             assert L.slg_tuning_set(key, lo - 1) != 0 and L.slg_tuning_set(key, hi + 1) != 0
-        assert L.slg_tuning_set(5, 0) != 0 and L.slg_tuning_set(-1, 0) != 0
+        assert L.slg_tuning_set(6, 0) != 0 and L.slg_tuning_set(-1, 0) != 0
     finally:
         for key, val in defaults.items():
             L.slg_tuning_set(key, val)

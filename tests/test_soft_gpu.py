@@ -380,3 +380,35 @@ def test_train_model_graphed_step_matches_eager(ctor):
     res = train_model(make(), X, y, X, y, dev, epochs=1, bs=128, val_every=1,
                       log=lambda *a: None, flip_p=0.05, cutout=3)
     assert 0.0 <= res["test_hard"] <= 100.0 and res["history"]["epoch"] == [1]
+
+
+@pytest.mark.parametrize("B", [37, 300])
+@pytest.mark.parametrize("k, sel", [(8, "softmax"), (5, "softmax"), (1, "softmax"), (8, "hard")])
+def test_multilinear6_conv_backward_kernels_agree(B, k, sel):
+    """One-level arity-6 multilinear conv trees: the factorised low-register backward
+    (tuning key 5 = 1) and the generic tree backward (key 5 = 0) give the same input,
+    connection and LUT gradients within the fp32 tolerance, for softmax and hard Top-K
+    selection, K below the template width, and batches that end inside a warp round."""
+    from silogic_b200 import _lib
+    L = _lib.lib()
+    kw = dict(in_channels=9, in_hw=12, channels=[16, 24], head_widths=[120, 60], tree_depth=1,
+              node="multilinear", arity=6, k=k, n_chan=4, gate_select=sel, tau=12.0, seed=2)
+    m = _rand_model("LogicConvNet", kw, 23).to(dev).train()
+    g = torch.Generator().manual_seed(B + k)
+    x = torch.rand(B, 9, 12, 12, generator=g)
+    rmat = torch.randn(B, 10, generator=g).to(dev)
+    grads = {}
+    try:
+        for key in (0, 1):
+            assert L.slg_tuning_set(5, key) == 0
+            m.zero_grad()
+            xd = x.to(dev).requires_grad_(True)
+            (m(xd) * rmat).sum().backward()
+            grads[key] = {"x": xd.grad.detach().cpu().numpy()}
+            grads[key].update({n: p.grad.detach().cpu().numpy() for n, p in m.named_parameters()
+                               if p.grad is not None})
+    finally:
+        L.slg_tuning_set(5, 1)
+    assert grads[0].keys() == grads[1].keys()
+    for name in grads[0]:
+        assert_grad_close(grads[1][name], grads[0][name], name)
