@@ -836,10 +836,14 @@ def main():
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip the reference's Triton path (timed in a child process, N=1 only)")
     ap.add_argument("--soft-only", action="store_true", help="profile the soft leg alone")
+    ap.add_argument("--soft-batch", type=int, default=None,
+                    help="soft fwd+bwd batch (default: the config's; smaller for profiling)")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the hard batch (small cases for profiling)")
     a = ap.parse_args()
     cfg = dict(CONFIGS[a.config])
+    if a.soft_batch:
+        cfg["soft_batch"] = a.soft_batch
     if a.batch:
         cfg["hard_batch"] = a.batch
         cfg["chunk"] = min(cfg.get("chunk", a.batch), a.batch)
