@@ -448,8 +448,26 @@ conv_soft_bwd_ml6_kernel(ConvArgs A, const float* __restrict__ gy, float* __rest
     const int p = tile * CS_WARPS + warp;
     float* wrow = ws + (((int64_t)blockIdx.y * tiles + tile) * A.n_out + n) * npart;
     conv_stage<N_MULTI, 6, 1>(S, A, n);
+    // tap table with stride KT per leaf (slots k >= K hold -1, weights 0), so every tap
+    // index below is a compile-time offset from the leaf's base
+    __shared__ float s_w[L * KT];
+    for (int e = threadIdx.x; e < L * KT; e += blockDim.x)
+        s_w[e] = (e % KT) < A.K ? S.w[(e / KT) * A.K + e % KT] : 0.f;
     int* pos = s_pos[warp];
-    if (p < npos) conv_fill_pos<N_MULTI, 6, 1, KT>(S, A, p / A.Wp, p % A.Wp, pos, lane);
+    if (p < npos) {
+        const int py = p / A.Wp, px = p % A.Wp, HW = A.H * A.W;
+        for (int i = lane; i < A.pool * A.pool * L * KT; i += 32) {
+            const int q = i / (L * KT), e8 = i % (L * KT), k = e8 % KT, e = (e8 / KT) * A.K + k;
+            int v = -1;
+            if (k < A.K) {
+                const int iy = py * A.pool + q / A.pool + S.tap_dy[e];
+                const int ix = px * A.pool + q % A.pool + S.tap_dx[e];
+                if (iy >= 0 && iy < A.H && ix >= 0 && ix < A.W) v = S.tap_c[e] * HW + iy * A.W + ix;
+            }
+            pos[i] = v;
+        }
+    }
+    __syncthreads();
     float* buf = ml6_buf + warp * ml6_rows<KT>() * ML6_ROW;
     float* bu = buf;                               // [8][ML6_ROW]   u
     float* bh = buf + 8 * ML6_ROW;                 // [8][ML6_ROW]   g * v
@@ -468,7 +486,6 @@ conv_soft_bwd_ml6_kernel(ConvArgs A, const float* __restrict__ gy, float* __rest
 
     if (p < npos) {
         const int64_t b0 = (int64_t)blockIdx.y * (32 * CS_ITER);
-        float vals[2 * L];
         for (int it = 0; it < CS_ITER; ++it) {
             if (b0 + it * 32 >= A.ldb) break;              // warp-uniform
             // lanes past the batch stay in the loop (the warp shares the buffer) and
@@ -476,16 +493,8 @@ conv_soft_bwd_ml6_kernel(ConvArgs A, const float* __restrict__ gy, float* __rest
             const bool live = b0 + it * 32 + lane < A.ldb;
             const int64_t b = live ? b0 + it * 32 + lane : b0;
             const float g = live ? gy[((n * npos) + p) * A.ldb + b] : 0.f;
-            int bq = 0;
-            if (A.pool > 1 && A.pool_arg) {
-                bq = A.pool_arg[((n * npos) + p) * A.ldb + b];
-            } else if (A.pool > 1) {
-                float best = 0.f;
-                for (int q = 0; q < A.pool * A.pool; ++q) {
-                    const float v = conv_tree_value<N_MULTI, 6, 1, KT>(S, A, pos + q * L * KT, b, vals);
-                    if (q == 0 || v > best) { best = v; bq = q; }
-                }
-            }
+            // pooled blocks come here only with the forward's saved window argmax
+            const int bq = A.pool > 1 ? A.pool_arg[((n * npos) + p) * A.ldb + b] : 0;
             const int* posq = pos + bq * L * KT;
             // leaf values; tap values go to the buffer for the connection gradients
             // one leaf at a time (KT loads in flight, not L*KT); each leaf value is shifted
@@ -494,14 +503,14 @@ conv_soft_bwd_ml6_kernel(ConvArgs A, const float* __restrict__ gy, float* __rest
 #pragma unroll 1
             for (int l = 0; l < L; ++l) {
                 float sl = 0.f;
+                const int* pl = posq + l * KT;
+                const float* wl = s_w + l * KT;
 #pragma unroll
                 for (int k = 0; k < KT; ++k) {
                     float v = 0.f;
-                    if (k < K) {
-                        const int pp = posq[l * K + k];
-                        if (pp >= 0 && live) v = __ldg(&A.x[(int64_t)pp * A.ldb + b]);
-                        sl += S.w[l * K + k] * v;
-                    }
+                    const int pp = pl[k];
+                    if (pp >= 0 && live) v = __ldg(&A.x[(int64_t)pp * A.ldb + b]);
+                    sl += wl[k] * v;
                     bx[(l * KT + k) * ML6_ROW + lane] = v;
                 }
 #pragma unroll
@@ -579,17 +588,16 @@ conv_soft_bwd_ml6_kernel(ConvArgs A, const float* __restrict__ gy, float* __rest
 #pragma unroll 1
             for (int l = 0; l < L; ++l) {
                 const float gl = bg[l * ML6_ROW + lane];
+                const int* pl = posq + l * KT;
+                const float* wl = s_w + l * KT;
 #pragma unroll
                 for (int k = 0; k < KT; ++k) {
-                    if (k < K) {
-                        const int e = l * K + k;
-                        const int pp = posq[e];
-                        if (pp >= 0 && live) {
-                            const int64_t idx = (int64_t)pp * A.ldb + b;
-                            if (A.gleaf)
-                                A.gleaf[((n * (L * K) + e) * (int64_t)npos + p) * A.ldb + b] = gl * S.w[e];
-                            else if (gx && S.w[e] != 0.0f) atomicAdd(&gx[idx], gl * S.w[e]);
-                        }
+                    const int pp = pl[k];
+                    const float wk = wl[k];
+                    if (pp >= 0 && live) {
+                        if (A.gleaf)
+                            A.gleaf[((n * (L * K) + l * K + k) * (int64_t)npos + p) * A.ldb + b] = gl * wk;
+                        else if (gx && wk != 0.0f) atomicAdd(&gx[(int64_t)pp * A.ldb + b], gl * wk);
                     }
                 }
             }
@@ -725,7 +733,7 @@ inline void conv_launch_bwd(const ConvArgs& A, const float* gy, float* gx, float
     bool done = false;
     if constexpr (NODE == N_MULTI && AR == 6 && D == 1 && KT <= 8) {
         // one-level 64-entry LUT trees (no wire residual): the low-register backward
-        if (A.wire_r == 0 && tuning(T_CONV_ML6) == 1 &&
+        if (A.wire_r == 0 && (A.pool == 1 || A.pool_arg) && tuning(T_CONV_ML6) == 1 &&
             cudaFuncSetAttribute(conv_soft_bwd_ml6_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  ml6_smem_bytes<KT>()) == cudaSuccess) {
             conv_soft_bwd_ml6_kernel<KT><<<grid, CS_WARPS * 32, ml6_smem_bytes<KT>(), st>>>(A, gy, gx, ws, npart);
