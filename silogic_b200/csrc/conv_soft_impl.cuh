@@ -54,6 +54,7 @@ struct ConvSmem {
     int tap_dy[L * CS_KMAX];
     int tap_dx[L * CS_KMAX];
     float w[L * CS_KMAX];
+    float wk[L * CS_KMAX];       // the same weights at stride KT per leaf, 0 past K
     float np[NODES * NodeStage<NODE, AR>::NPS];
 };
 
@@ -114,19 +115,34 @@ __device__ __forceinline__ void conv_stage(ConvSmem<NODE, AR, D>& S, const ConvA
     __syncthreads();
 }
 
-// Tap positions of one warp's pool window: pos[q*L*KT + l*K + k] = c*H*W + iy*W + ix of
-// candidate k of leaf l at window element q, or -1 outside the image.  Warp-uniform,
-// so it is computed once per warp and reused for every sample of the chunk.
+// S.wk[l*KT + k] = S.w[l*K + k] for k < K, else 0: with the position table below it
+// makes every tap index a compile-time offset from its leaf's base.  Whole block; call
+// after conv_stage.
+template <int NODE, int AR, int D, int KT>
+__device__ __forceinline__ void conv_stage_wk(ConvSmem<NODE, AR, D>& S, const ConvArgs& A) {
+    constexpr int L = TreeShape<AR, D>::L;
+    for (int e = threadIdx.x; e < L * KT; e += blockDim.x)
+        S.wk[e] = (e % KT) < A.K ? S.w[(e / KT) * A.K + e % KT] : 0.f;
+    __syncthreads();
+}
+
+// Tap positions of one warp's pool window: pos[q*L*KT + l*KT + k] = c*H*W + iy*W + ix of
+// candidate k of leaf l at window element q, or -1 outside the image or for k >= K.
+// Warp-uniform, so it is computed once per warp and reused for every sample of the chunk.
 template <int NODE, int AR, int D, int KT>
 __device__ __forceinline__ void conv_fill_pos(const ConvSmem<NODE, AR, D>& S, const ConvArgs& A, int py,
                                               int px, int* pos, int lane) {
     constexpr int L = TreeShape<AR, D>::L;
     const int K = A.K, HW = A.H * A.W;
-    for (int i = lane; i < A.pool * A.pool * L * K; i += 32) {
-        const int q = i / (L * K), e = i % (L * K);
-        const int y = py * A.pool + q / A.pool, x = px * A.pool + q % A.pool;
-        const int iy = y + S.tap_dy[e], ix = x + S.tap_dx[e];
-        pos[q * L * KT + e] = (iy >= 0 && iy < A.H && ix >= 0 && ix < A.W) ? S.tap_c[e] * HW + iy * A.W + ix : -1;
+    for (int i = lane; i < A.pool * A.pool * L * KT; i += 32) {
+        const int q = i / (L * KT), e8 = i % (L * KT), k = e8 % KT, e = (e8 / KT) * K + k;
+        int v = -1;
+        if (k < K) {
+            const int y = py * A.pool + q / A.pool, x = px * A.pool + q % A.pool;
+            const int iy = y + S.tap_dy[e], ix = x + S.tap_dx[e];
+            if (iy >= 0 && iy < A.H && ix >= 0 && ix < A.W) v = S.tap_c[e] * HW + iy * A.W + ix;
+        }
+        pos[i] = v;
     }
     __syncwarp();
 }
@@ -146,15 +162,13 @@ __device__ __forceinline__ float conv_tree_value(const ConvSmem<NODE, AR, D>& S,
 #pragma unroll
         for (int k = 0; k < KT; ++k) {
             if (taps) taps[l * KT + k] = 0.f;
-            if (k < K) {
-                const int p = posq[l * K + k];
-                // zero weights (one-hot straight-through selection) contribute nothing to the
-                // value: skip the load unless the backward wants the tap
-                if (p >= 0 && (taps || S.w[l * K + k] != 0.0f)) {
-                    const float v = __ldg(&A.x[(int64_t)p * A.ldb + b]);
-                    s += S.w[l * K + k] * v;
-                    if (taps) taps[l * KT + k] = v;
-                }
+            const int p = posq[l * KT + k];
+            // zero weights (one-hot straight-through selection, slots past K) contribute
+            // nothing to the value: skip the load unless the backward wants the tap
+            if (p >= 0 && (taps || S.wk[l * KT + k] != 0.0f)) {
+                const float v = __ldg(&A.x[(int64_t)p * A.ldb + b]);
+                s += S.wk[l * KT + k] * v;
+                if (taps) taps[l * KT + k] = v;
             }
         }
         vals[l] = s;
@@ -192,10 +206,10 @@ __device__ __forceinline__ float4 conv_tree_value4(const ConvSmem<NODE, AR, D>& 
         float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int k = 0; k < KT; ++k) {
-            if (k < K && S.w[l * K + k] != 0.0f) {
-                const int p = posq[l * K + k];
+            if (S.wk[l * KT + k] != 0.0f) {
+                const int p = posq[l * KT + k];
                 if (p >= 0) {
-                    const float w = S.w[l * K + k];
+                    const float w = S.wk[l * KT + k];
                     const float4 v = __ldg(reinterpret_cast<const float4*>(A.x + (int64_t)p * A.ldb + b4));
                     s.x += w * v.x; s.y += w * v.y; s.z += w * v.z; s.w += w * v.w;
                 }
@@ -237,7 +251,10 @@ conv_soft_fwd_kernel(ConvArgs A, float* __restrict__ y) {
     const int lane = threadIdx.x & 31;
     __shared__ int s_pos[CS_WARPS][4 * L * KT];
     const bool wired = n < A.wire_r;
-    if (!wired) conv_stage<NODE, AR, D>(S, A, n);
+    if (!wired) {
+        conv_stage<NODE, AR, D>(S, A, n);
+        conv_stage_wk<NODE, AR, D, KT>(S, A);
+    }
     if (p >= npos) return;
     const int py = p / A.Wp, px = p % A.Wp;
     int* pos = s_pos[threadIdx.x >> 5];
@@ -305,6 +322,7 @@ conv_soft_bwd_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict
         return;
     }
     conv_stage<NODE, AR, D>(S, A, n);
+    conv_stage_wk<NODE, AR, D, KT>(S, A);
     __shared__ int s_pos[CS_WARPS][4 * L * KT];
     int* pos = s_pos[warp];
     if (p < npos) conv_fill_pos<NODE, AR, D, KT>(S, A, p / A.Wp, p % A.Wp, pos, lane);
@@ -377,8 +395,9 @@ conv_soft_bwd_kernel(ConvArgs A, const float* __restrict__ gy, float* __restrict
                 for (int k = 0; k < KT; ++k) {
                     if (k < K) {
                         const int e = l * K + k;
-                        if (posq[e] >= 0) {
-                            const int64_t idx = (int64_t)posq[e] * A.ldb + b;
+                        const int pp = posq[l * KT + k];
+                        if (pp >= 0) {
+                            const int64_t idx = (int64_t)pp * A.ldb + b;
                             acc_w[l * KT + k] += gl * (KEEP ? taps[l * KT + k] : __ldg(&A.x[idx]));
                             if (A.gleaf)
                                 A.gleaf[((n * (L * K) + e) * (int64_t)npos + p) * A.ldb + b] = gl * S.w[e];
